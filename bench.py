@@ -1,0 +1,473 @@
+"""Benchmark of the NVFP4 hot paths on B200; prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+
+Default workload: configuration 1 (dual GEMM M=8192 N=14336 K=4096, the
+compute-bound SiLU-gated FFN shape).  A step is one dual-GEMM call over one
+batch of synthetic inputs (seeded N(0,1) operands quantised to NVFP4).
+
+* value: device time of the K timed calls (CUDA events on the launching
+  stream, L2 flushed between calls outside the events), max over ranks;
+  whole-job effective TFLOP/s = all ranks' FLOP / that time.
+* e2e: the same metric through the public drop-in ``custom_kernel`` with the
+  step's inputs copied from pinned host memory and the output copied back,
+  inside the timed region.
+* roofline: dominant kernel's achieved FLOP/s (or GB/s) against the NVFP4
+  dense peak (4x the measured bf16 peak) or the measured HBM copy bandwidth.
+* cpu_baseline / --impl reference: the CPU oracle (dequantise + fp32 matmul,
+  the reference's ref_kernel restated) on a bounded sample of the workload.
+
+Multi-GPU (torchrun, one rank per GPU): dual GEMM is sharded along N with the
+per-rank shard fixed at the configuration's N (weak scaling, no collective on
+the data path); grouped configurations assign experts by LPT (strong scaling).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (str(ROOT / "blackwell-nvfp4-kernels_b200"), str(ROOT)):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+L2_FLUSH_BYTES = 512 << 20
+
+
+# ---------------------------------------------------------------------------
+# workload
+# ---------------------------------------------------------------------------
+def dual_workload(cfg: int, rank: int, world: int, device):
+    """Rank's dual GEMM: A replicated (same seed everywhere), B1/B2 = this
+    rank's N-shard of a global N = N_cfg * world (weak scaling)."""
+    from nvfp4_b200 import inputs as I
+    spec = I.DUAL_CONFIGS[cfg]
+    m, n, k = spec["m"], spec["n"], spec["k"]
+    ga = torch.Generator().manual_seed(spec["seed"])
+    a = torch.randn(m, k, generator=ga)
+    gb = torch.Generator().manual_seed(spec["seed"] * 1000 + rank)
+    if rank == 0:   # rank 0's shard is exactly the single-GPU configuration
+        gb = torch.Generator().manual_seed(spec["seed"])
+        torch.randn(m, k, generator=gb)
+    b1 = torch.randn(n, k, generator=gb)
+    b2 = torch.randn(n, k, generator=gb)
+    data = I.dual_from_fp32(a, b1, b2, device=device)
+    flop = 4.0 * m * n * k
+    nbytes = m * k // 2 + 2 * n * k // 2 + (m + 2 * n) * k // 16 + 2 * m * n
+    desc = dict(workload=f"dual_gemm_cfg{cfg}", m=m, n_per_rank=n, n_global=n * world, k=k, l=1)
+    return data, flop, nbytes, desc
+
+
+def group_workload(cfg: int, rank: int, world: int, device):
+    from nvfp4_b200 import inputs as I
+    from nvfp4_b200.shard import imbalance, lpt_assign
+    spec = I.GROUP_CONFIGS[cfg]
+    ms = I.config3_m_sizes(spec["seed"], spec["groups"]) if cfg == 3 else \
+        I.config4_m_sizes(spec["seed"], spec["experts"], spec["tokens"], spec["zipf_s"])
+    n, k = spec["n"], spec["k"]
+    costs = [float(m) * n * k for m in ms]
+    bins = lpt_assign(costs, world)
+    mine = bins[rank]
+    g = torch.Generator().manual_seed(1000 + spec["seed"])
+    pairs = []
+    for i, m in enumerate(ms):   # draw every group so data is identical for any world size
+        a = torch.randn(m, k, generator=g)
+        b = torch.randn(n, k, generator=g)
+        if i in mine:
+            pairs.append((a, b))
+    data = I.group_from_fp32(pairs, device=device)
+    mr = [ms[i] for i in mine]
+    flop = sum(2.0 * m * n * k for m in mr)
+    nbytes = sum(m * k // 2 + m * k // 16 + 2 * m * n + n * k // 2 + n * k // 16 for m in mr)
+    desc = dict(workload=f"grouped_gemm_cfg{cfg}", groups=len(ms), groups_this_rank=len(mine),
+                sum_m=sum(ms), n=n, k=k, lpt_imbalance=round(imbalance(costs, bins), 4))
+    return data, flop, nbytes, desc
+
+
+def make_workload(cfg, rank, world, device):
+    return dual_workload(cfg, rank, world, device) if cfg in (0, 1, 2) else \
+        group_workload(cfg, rank, world, device)
+
+
+def call(cfg, data):
+    if cfg in (0, 1, 2):
+        from nvfp4_b200.dual_gemm import custom_kernel
+    else:
+        from nvfp4_b200.group_gemm import custom_kernel
+    return custom_kernel(data)
+
+
+def device_tensors(cfg, data):
+    """(input tensors a user would ship each step, output tensors)."""
+    if cfg in (0, 1, 2):
+        return [data[0], data[1], data[2], data[6], data[7], data[8]], [data[9]]
+    abc, _, perm, sizes = data
+    ins, outs = [], []
+    for (a, b, c), (sa, sb), s in zip(abc, perm, sizes):
+        if s[0] > 0:
+            ins += [a, sa]
+            outs.append(c)
+        ins += [b, sb]
+    return ins, outs
+
+
+def nbytes_of(ts):
+    return sum(t.numel() * t.element_size() for t in ts)
+
+
+# ---------------------------------------------------------------------------
+# clocks (NVML, read-only)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
+
+    def __init__(self, device_index: int, period_s: float = 0.01):
+        self.samples, self.reasons = [], set()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = self._handle(pynvml, device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # noqa: BLE001
+            self.err = repr(e)
+        self.period = period_s
+        self._stop = threading.Event()
+
+    @staticmethod
+    def _handle(nv, device_index):
+        """NVML handle of the CUDA device (matched by PCI id, so it also works
+        under CUDA_VISIBLE_DEVICES)."""
+        try:
+            pr = torch.cuda.get_device_properties(device_index)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            return nv.nvmlDeviceGetHandleByPciBusId_v2(bus)
+        except Exception:  # noqa: BLE001
+            return nv.nvmlDeviceGetHandleByIndex(device_index)
+
+    def _reasons(self):
+        nv = self.nv
+        fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
+        return fn(self.h)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                bits = self._reasons()
+                for name, b in self.REASONS.items():
+                    if bits & b:
+                        self.reasons.add(name)
+            except Exception:  # noqa: BLE001
+                pass
+            time.sleep(self.period)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": self.err}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# CPU oracle timing
+# ---------------------------------------------------------------------------
+def cpu_sample_step(cfg, data_cpu, rows, cols):
+    """One bounded sample of the workload through the oracle: `rows` output
+    rows x `cols` output columns (dual) or the same block of one group."""
+    from oracle import nvfp4_oracle as O
+    if cfg in (0, 1, 2):
+        a, b1, b2, sfa, sfb1, sfb2 = data_cpu
+        O.ref_dual(a[:rows], b1[:cols], b2[:cols], sfa[:rows], sfb1[:cols], sfb2[:cols])
+        return 4.0 * rows * cols * a.shape[1] * 2
+    a, b, sfa, sfb = data_cpu
+    O.ref_group(a[:rows], b[:cols], sfa[:rows], sfb[:cols])
+    return 2.0 * rows * cols * a.shape[1] * 2
+
+
+def cpu_inputs(cfg, data):
+    u8 = lambda t: t.detach().cpu().view(torch.uint8).numpy()[:, :, 0]
+    if cfg in (0, 1, 2):
+        return [u8(t) for t in data[:6]]
+    abc, sfab, _, sizes = data
+    i = max(range(len(sizes)), key=lambda j: sizes[j][0])   # largest group
+    return [u8(abc[i][0]), u8(abc[i][1]), u8(sfab[i][0]), u8(sfab[i][1])]
+
+
+def cpu_sample_shape(cfg, data_cpu):
+    rows = min(data_cpu[0].shape[0], 2048)
+    cols = min(data_cpu[1].shape[0], 2048)
+    return rows, cols
+
+
+def time_cpu(cfg, data_cpu, budget_s: float, min_reps: int = 1):
+    rows, cols = cpu_sample_shape(cfg, data_cpu)
+    cpu_sample_step(cfg, data_cpu, min(rows, 64), min(cols, 64))     # warm caches / threads
+    flops, secs, reps = 0.0, 0.0, 0
+    while reps < min_reps or secs < budget_s:
+        t0 = time.perf_counter()
+        flops += cpu_sample_step(cfg, data_cpu, rows, cols)
+        secs += time.perf_counter() - t0
+        reps += 1
+    return flops / secs / 1e12, reps, rows, cols
+
+
+def cpu_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count()
+
+
+# ---------------------------------------------------------------------------
+# main
+# ---------------------------------------------------------------------------
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), float(d["bf16_tflops"]), "measured"
+    return FALLBACK_PEAKS["hbm_gbs"], FALLBACK_PEAKS["bf16_tflops"], "fallback"
+
+
+def load_traffic(workload: str):
+    p = ROOT / "profiles" / "traffic.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        v = d.get(workload)
+        if v is not None:
+            return float(v["dram_bytes_per_launch"])
+    return None
+
+
+def metric_name(cfg):
+    return "NVFP4 effective TFLOPS (dual GEMM)" if cfg in (0, 1, 2) else \
+        "NVFP4 effective TFLOPS (grouped GEMM)"
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    assert args.warmup >= 3 or args.impl == "reference", "need >= 3 warm-up steps"
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    cfg = args.config
+
+    if args.impl == "reference":
+        return run_reference_arm(args, cfg, rank, world)
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+        pg = dist
+
+    from nvfp4_b200 import _lib
+    data, flop, nbytes, desc = make_workload(cfg, rank, world, device)
+    stream = torch.cuda.current_stream(device)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+
+    for _ in range(args.warmup):
+        call(cfg, data)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        for i in range(args.steps):
+            flush.zero_()                       # evict L2 between calls (outside the events)
+            starts[i].record(stream)
+            call(cfg, data)
+            ends[i].record(stream)
+        torch.cuda.synchronize()
+    if pg:
+        pg.barrier()
+    status = _lib.device_status()
+    assert status == 0, f"device status {status:#x}"
+    per_call_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    t_total = torch.tensor([sum(per_call_ms)], dtype=torch.float64, device=device)
+    flop_t = torch.tensor([flop], dtype=torch.float64, device=device)
+    if pg:
+        pg.all_reduce(t_total, op=pg.ReduceOp.MAX)
+        pg.all_reduce(flop_t, op=pg.ReduceOp.SUM)
+    t_max_s = t_total.item() / 1e3
+    total_flop = flop_t.item() * args.steps
+    value = total_flop / t_max_s / 1e12
+    ms_per_step = t_max_s * 1e3 / args.steps
+
+    # ---- e2e through the public API with pinned host buffers
+    ins, outs = device_tensors(cfg, data)
+    h_ins = [t.detach().cpu().pin_memory() for t in ins]
+    h_outs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outs]
+    h2d, d2h = nbytes_of(ins), nbytes_of(outs)
+    call(cfg, data)
+    torch.cuda.synchronize()
+    es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if pg:
+        pg.barrier()
+    torch.cuda.synchronize()
+    es.record(stream)
+    for _ in range(args.e2e_steps):
+        for d, h in zip(ins, h_ins):
+            d.copy_(h, non_blocking=True)
+        call(cfg, data)
+        for h, d in zip(h_outs, outs):
+            h.copy_(d, non_blocking=True)
+    ee.record(stream)
+    torch.cuda.synchronize()
+    e2e_t = torch.tensor([es.elapsed_time(ee) / 1e3], dtype=torch.float64, device=device)
+    if pg:
+        pg.all_reduce(e2e_t, op=pg.ReduceOp.MAX)
+    e2e_value = flop_t.item() * args.e2e_steps / e2e_t.item() / 1e12
+
+    # ---- roofline of the dominant kernel (the GEMM kernel is the only launch)
+    hbm_peak, bf16_peak, peak_kind = load_peaks()
+    nvfp4_peak = 4.0 * bf16_peak
+    avg_launch_s = statistics.mean(per_call_ms) / 1e3
+    hbm_bound = cfg == 2
+    traffic = load_traffic(desc["workload"])
+    if hbm_bound:
+        ach = nbytes / avg_launch_s / 1e9
+        roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(ach / hbm_peak, 4)}
+    else:
+        ach = flop / avg_launch_s / 1e12
+        roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": nvfp4_peak,
+                "unit": "TFLOP/s", "frac": round(ach / nvfp4_peak, 4)}
+    roof["traffic"] = traffic
+    roof["algorithmic_bytes"] = nbytes
+    roof["peak_source"] = (f"{peak_kind}: NVFP4 dense = 4 x bf16 {bf16_peak} TFLOP/s"
+                           if not hbm_bound else f"{peak_kind}: HBM copy {hbm_peak} GB/s")
+
+    result = {
+        "metric": metric_name(cfg), "value": round(value, 2), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5), "us_per_call": round(ms_per_step * 1e3, 2),
+        "higher_is_better": True, "scaling": "weak" if cfg in (0, 1, 2) else "strong",
+        "vs_baseline": None, "dtype": "nvfp4(e2m1+e4m3 block16) x nvfp4 -> fp32 acc -> fp16",
+        "data": "synthetic: seeded N(0,1) fp32 quantised to NVFP4",
+        "config": {**desc, "parallelism": f"{'n-shard' if cfg in (0, 1, 2) else 'expert-lpt'}{world}",
+                   "l2": f"flushed ({L2_FLUSH_BYTES >> 20} MiB write) between timed calls"},
+        "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
+                "api": "nvfp4_b200.*.custom_kernel (ctypes -> libnvfp4_b200.so)"},
+        "roofline": roof,
+        "gpu_launches": args.steps,
+        "clocks": clk.summary(),
+    }
+
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        dc = cpu_inputs(cfg, data)
+        torch.set_num_threads(cpu_cores())
+        v, reps, rows, cols = time_cpu(cfg, dc, args.cpu_budget)
+        result["cpu_baseline"] = {
+            "value": round(v, 5), "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port",
+            "sample": f"oracle ref ({'dual' if cfg < 3 else 'group'}) on a {rows}x{cols} output "
+                      f"block x K={dc[0].shape[1] * 2}, {reps} reps (~{args.cpu_budget:.0f} s)"}
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def run_reference_arm(args, cfg, rank, world):
+    """The reference's CPU path (its ref_kernel restated as the numpy oracle)
+    on the host cores: rank 0 only; other ranks exit without work."""
+    if rank != 0:
+        return
+    from nvfp4_b200 import inputs as I
+    if cfg in (0, 1, 2):
+        spec = I.DUAL_CONFIGS[cfg]
+        g = torch.Generator().manual_seed(spec["seed"])
+        rows, cols = min(spec["m"], 2048), min(spec["n"], 2048)
+        k = spec["k"]
+        a = torch.randn(spec["m"], k, generator=g)[:rows]
+        b1 = torch.randn(spec["n"], k, generator=g)[:cols]
+        b2 = torch.randn(spec["n"], k, generator=g)[:cols]
+        d = I.dual_from_fp32(a, b1, b2, device="cpu")
+        dc = [t.view(torch.uint8).numpy()[:, :, 0] for t in d[:6]]
+        wl = f"dual_gemm_cfg{cfg}"
+    else:
+        d = I.group_config_input(cfg, device="cpu") if cfg == 3 else None
+        if d is None:   # config 4: largest expert only
+            ms = I.config4_m_sizes()
+            spec = I.GROUP_CONFIGS[4]
+            gen = torch.Generator().manual_seed(7)
+            mbig = min(max(ms), 2048)
+            d = I.group_from_fp32([(torch.randn(mbig, spec["k"], generator=gen),
+                                    torch.randn(spec["n"], spec["k"], generator=gen))], device="cpu")
+        dc = cpu_inputs(cfg, d)
+        wl = f"grouped_gemm_cfg{cfg}"
+    torch.set_num_threads(cpu_cores())
+    rows, cols = cpu_sample_shape(cfg, dc)
+    for _ in range(args.warmup):
+        cpu_sample_step(cfg, dc, rows, cols)
+    budget = max(0.0, 150.0 / max(1, args.steps))
+    flops, secs = 0.0, 0.0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        flops += cpu_sample_step(cfg, dc, rows, cols)
+        secs += time.perf_counter() - t0
+    v = flops / secs / 1e12
+    sample = (f"numpy oracle (dequantise + fp32 matmul) on a {rows}x{cols} output block "
+              f"x K={dc[0].shape[1] * 2} per step")
+    print(json.dumps({
+        "impl": "reference", "metric": metric_name(cfg), "value": round(v, 5), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(secs * 1e3 / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak" if cfg in (0, 1, 2) else "strong", "vs_baseline": None,
+        "dtype": "fp32 (dequantised nvfp4)", "data": "synthetic: seeded N(0,1) quantised to NVFP4",
+        "config": {"workload": wl, "sample_rows": rows, "sample_cols": cols, "budget_s": budget},
+        "cpu_baseline": {"value": round(v, 5), "unit": "TFLOP/s", "cores": cpu_cores(),
+                         "kind": "port", "sample": sample},
+        "e2e": {"value": round(v, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,326 @@
+// C ABI of libnvfp4_b200.so: argument validation, TMA descriptor encoding,
+// tile-configuration choice and kernel launches for the NVFP4 dual and
+// grouped GEMMs.  See include/nvfp4_b200.h for the contract.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <vector>
+
+#include "../../include/nvfp4_b200.h"
+#include "dual_gemm.cuh"
+#include "grouped_gemm.cuh"
+
+namespace nvfp4 {
+
+// Per-device status word written by the kernels' bounded waits.
+__device__ unsigned g_status_word;
+
+__global__ void wait_selftest_kernel(unsigned* status, long long limit) {
+  __shared__ uint64_t bar;
+  __shared__ volatile int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    abort_flag = 0;
+    fence_barrier_init();
+  }
+  __syncthreads();
+  const AbortCtl ctl{&abort_flag, status, limit};
+  if (threadIdx.x == 0) ctl.wait(smem_u32(&bar), 0, kDevTimeoutSelftest);  // nobody arrives
+}
+
+namespace {
+
+thread_local char t_last_error[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(t_last_error, sizeof(t_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+constexpr int kMaxDevices = 64;
+
+struct DeviceState {
+  bool ready = false;
+  int num_sms = 0;
+  unsigned* status = nullptr;
+  bool smem_set[16] = {};
+};
+
+std::mutex g_mu;
+DeviceState g_dev[kMaxDevices];
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+long long wait_limit_cycles() {
+  static long long v = [] {
+    const char* e = getenv("NVFP4_WAIT_LIMIT_CYCLES");
+    long long x = e ? atoll(e) : 0;
+    return x > 0 ? x : 4000000000LL;  // ~2 s at 2 GHz
+  }();
+  return v;
+}
+
+int env_int(const char* name, int dflt) {
+  const char* e = getenv(name);
+  return e ? atoi(e) : dflt;
+}
+
+// Resolve per-device state (SM count, status-word address) once.
+int get_device(DeviceState** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_DEVICE, "device index %d", dev);
+  std::lock_guard<std::mutex> lk(g_mu);
+  DeviceState& d = g_dev[dev];
+  if (!d.ready) {
+    int major = 0, minor = 0;
+    cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+    cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+    if (major != 10 || minor != 0)
+      return fail(NVFP4_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a",
+                  dev, major, minor);
+    e = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "SM count: %s", cudaGetErrorString(e));
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_status_word);
+    if (e != cudaSuccess)
+      return fail(NVFP4_ERR_CUDA, "status word address: %s", cudaGetErrorString(e));
+    d.status = static_cast<unsigned*>(p);
+    if (!g_encode) {
+      cudaDriverEntryPointQueryResult q;
+      void* fn = nullptr;
+      e = cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &fn, 12000,
+                                           cudaEnableDefault, &q);
+      if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn)
+        return fail(NVFP4_ERR_CUDA, "cuTensorMapEncodeTiled entry point unavailable");
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+    d.ready = true;
+  }
+  *out = &d;
+  return NVFP4_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// 3-D byte view [L][rows][K/2] of a packed e2m1 operand, box {128 B, box_rows, 1},
+// 128-byte swizzle (the canonical K-major SW128 operand layout of tcgen05.mma).
+int encode_operand(CUtensorMap* map, const void* base, int rows, int k, int l, int box_rows) {
+  const cuuint64_t dims[3] = {(cuuint64_t)(k / 2), (cuuint64_t)rows, (cuuint64_t)l};
+  const cuuint64_t strides[2] = {(cuuint64_t)(k / 2), (cuuint64_t)rows * (cuuint64_t)(k / 2)};
+  const cuuint32_t box[3] = {128u, (cuuint32_t)box_rows, 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(NVFP4_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%d k=%d l=%d", (int)r,
+                rows, k, l);
+  return NVFP4_OK;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+  return NVFP4_OK;
+}
+
+template <typename Kern>
+int set_smem_once(DeviceState* d, int slot, Kern kern, int bytes) {
+  if (d->smem_set[slot]) return NVFP4_OK;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess)
+    return fail(NVFP4_ERR_CUDA, "cudaFuncSetAttribute(smem=%d): %s", bytes, cudaGetErrorString(e));
+  d->smem_set[slot] = true;
+  return NVFP4_OK;
+}
+
+// ---------------------------------------------------------------- dual GEMM
+template <int kBN, int kStages, int kEpiWarps, int kAccBufs>
+int launch_dual(DeviceState* d, int slot, DualParams& p, cudaStream_t stream) {
+  using Cfg = DualCfg<kBN, kStages, kEpiWarps, kAccBufs>;
+  auto kern = dual_gemm_kernel<kBN, kStages, kEpiWarps, kAccBufs>;
+  int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
+  if (rc) return rc;
+  p.n_blocks = (p.n + kBN - 1) / kBN;
+  p.tiles = p.l * p.m_blocks * p.n_blocks;
+  const int grid = p.tiles < d->num_sms ? p.tiles : d->num_sms;
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  return check_launch("dual_gemm_kernel");
+}
+
+// ---------------------------------------------------------------- grouped GEMM
+template <int kMaxGroups>
+int launch_grouped_chunk(DeviceState* d, const nvfp4_group* gs, const int* idx, int count,
+                         cudaStream_t stream) {
+  constexpr int kBN = 128, kStages = 6;
+  using Cfg = GroupedCfg<kBN, kStages>;
+  auto kern = grouped_gemm_kernel<kBN, kStages, kMaxGroups>;
+  int rc = set_smem_once(d, kMaxGroups == 16 ? 8 : 9, kern, Cfg::kSmemBytes);
+  if (rc) return rc;
+  static thread_local GroupedParams<kMaxGroups> p;
+  int tiles = 0;
+  for (int i = 0; i < count; ++i) {
+    const nvfp4_group& g = gs[idx[i]];
+    GroupInfo& gi = p.g[i];
+    gi.sfa = static_cast<const uint8_t*>(g.sfa_perm);
+    gi.sfb = static_cast<const uint8_t*>(g.sfb_perm);
+    gi.c = static_cast<__half*>(g.c);
+    gi.m = g.m, gi.n = g.n, gi.k = g.k, gi.l = g.l;
+    gi.m_blocks = (g.m + kBM - 1) / kBM;
+    gi.n_blocks = (g.n + kBN - 1) / kBN;
+    gi.tile_start = tiles;
+    gi.pad_ = 0;
+    tiles += g.l * gi.m_blocks * gi.n_blocks;
+    if ((rc = encode_operand(&p.tmap_a[i], g.a, g.m, g.k, g.l, kBM))) return rc;
+    if ((rc = encode_operand(&p.tmap_b[i], g.b, g.n, g.k, g.l, kBN))) return rc;
+  }
+  p.num_groups = count;
+  p.tiles = tiles;
+  p.status = d->status;
+  p.wait_limit = wait_limit_cycles();
+  const int grid = tiles < d->num_sms ? tiles : d->num_sms;
+  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  return check_launch("grouped_gemm_kernel");
+}
+
+}  // namespace
+}  // namespace nvfp4
+
+using namespace nvfp4;
+
+extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, const void* sfa,
+                               const void* sfb1, const void* sfb2, void* c, int m, int n, int k,
+                               int l, void* stream_) {
+  if (!a || !b1 || !b2 || !sfa || !sfb1 || !sfb2 || !c)
+    return fail(NVFP4_ERR_INVALID_ARG, "null pointer argument");
+  if (m < 1 || n < 1 || k < 1 || l < 1)
+    return fail(NVFP4_ERR_INVALID_ARG, "sizes must be positive (m=%d n=%d k=%d l=%d)", m, n, k, l);
+  if (k % kBK != 0) return fail(NVFP4_ERR_SHAPE, "K=%d is not a multiple of 256", k);
+  if (n % 8 != 0) return fail(NVFP4_ERR_SHAPE, "N=%d is not a multiple of 8", n);
+  if ((long long)m * n * l >= (1LL << 40) || (long long)(m > n ? m : n) * k * l >= (1LL << 41))
+    return fail(NVFP4_ERR_SHAPE, "problem too large");
+  if (!aligned16(a) || !aligned16(b1) || !aligned16(b2) || !aligned16(sfa) || !aligned16(sfb1) ||
+      !aligned16(sfb2) || !aligned16(c))
+    return fail(NVFP4_ERR_ALIGNMENT, "all operands must be 16-byte aligned");
+  DeviceState* d = nullptr;
+  int rc = get_device(&d);
+  if (rc) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+
+  DualParams p;
+  memset(&p, 0, sizeof(p));
+  p.sfa = static_cast<const uint8_t*>(sfa);
+  p.sfb1 = static_cast<const uint8_t*>(sfb1);
+  p.sfb2 = static_cast<const uint8_t*>(sfb2);
+  p.c = static_cast<__half*>(c);
+  p.m = m, p.n = n, p.k = k, p.l = l;
+  p.m_blocks = (m + kBM - 1) / kBM;
+  p.k_blocks = k / kBK;
+  p.group_m = env_int("NVFP4_DUAL_GROUP_M", 16);
+  if (p.group_m < 1) p.group_m = 1;
+  p.status = d->status;
+  p.wait_limit = wait_limit_cycles();
+
+  // Tile choice: 128-wide tiles keep the tensor core fed from shared memory;
+  // when they would leave SMs idle, 64-wide tiles double the tile count.
+  const int tiles128 = l * p.m_blocks * ((n + 127) / 128);
+  int bn = tiles128 >= 2 * d->num_sms ? 128 : 64;
+  const int forced = env_int("NVFP4_DUAL_BN", 0);
+  if (forced == 64 || forced == 128) bn = forced;
+  if ((rc = encode_operand(&p.tmap_a, a, m, k, l, kBM))) return rc;
+  if ((rc = encode_operand(&p.tmap_b1, b1, n, k, l, bn))) return rc;
+  if ((rc = encode_operand(&p.tmap_b2, b2, n, k, l, bn))) return rc;
+  if (bn == 128) return launch_dual<128, 4, 8, 1>(d, 0, p, stream);
+  return launch_dual<64, 5, 4, 2>(d, 1, p, stream);
+}
+
+extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream_) {
+  if (!groups || num_groups < 0) return fail(NVFP4_ERR_INVALID_ARG, "bad group table");
+  std::vector<int> live;
+  live.reserve(num_groups);
+  for (int i = 0; i < num_groups; ++i) {
+    const nvfp4_group& g = groups[i];
+    if (g.m < 0 || g.n < 1 || g.k < 1 || g.l < 1)
+      return fail(NVFP4_ERR_INVALID_ARG, "group %d: bad sizes (m=%d n=%d k=%d l=%d)", i, g.m, g.n,
+                  g.k, g.l);
+    if (g.m == 0) continue;
+    if (!g.a || !g.b || !g.sfa_perm || !g.sfb_perm || !g.c)
+      return fail(NVFP4_ERR_INVALID_ARG, "group %d: null pointer", i);
+    if (g.k % kBK != 0) return fail(NVFP4_ERR_SHAPE, "group %d: K=%d not a multiple of 256", i, g.k);
+    if (g.n % 8 != 0) return fail(NVFP4_ERR_SHAPE, "group %d: N=%d not a multiple of 8", i, g.n);
+    if ((long long)g.m * g.n * g.l >= (1LL << 40))
+      return fail(NVFP4_ERR_SHAPE, "group %d: too large", i);
+    if (!aligned16(g.a) || !aligned16(g.b) || !aligned16(g.sfa_perm) || !aligned16(g.sfb_perm) ||
+        !aligned16(g.c))
+      return fail(NVFP4_ERR_ALIGNMENT, "group %d: operands must be 16-byte aligned", i);
+    live.push_back(i);
+  }
+  if (live.empty()) return NVFP4_OK;
+  DeviceState* d = nullptr;
+  int rc = get_device(&d);
+  if (rc) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const int n = (int)live.size();
+  if (n <= 16) return launch_grouped_chunk<16>(d, groups, live.data(), n, stream);
+  for (int s = 0; s < n; s += 96) {
+    const int cnt = n - s < 96 ? n - s : 96;
+    if ((rc = launch_grouped_chunk<96>(d, groups, live.data() + s, cnt, stream))) return rc;
+  }
+  return NVFP4_OK;
+}
+
+extern "C" int nvfp4_device_status(void* stream_, unsigned* bits_out) {
+  DeviceState* d = nullptr;
+  int rc = get_device(&d);
+  if (rc) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  cudaError_t e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "stream sync: %s", cudaGetErrorString(e));
+  unsigned bits = 0;
+  e = cudaMemcpy(&bits, d->status, sizeof(bits), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "status read: %s", cudaGetErrorString(e));
+  if (bits) {
+    const unsigned zero = 0;
+    cudaMemcpy(d->status, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+  }
+  if (bits_out) *bits_out = bits;
+  if (bits) return fail(NVFP4_ERR_TIMEOUT, "device status bits 0x%x (a bounded wait ran out)", bits);
+  return NVFP4_OK;
+}
+
+extern "C" int nvfp4_wait_selftest(long long limit_cycles, void* stream_) {
+  if (limit_cycles < 1) return fail(NVFP4_ERR_INVALID_ARG, "limit must be positive");
+  DeviceState* d = nullptr;
+  int rc = get_device(&d);
+  if (rc) return rc;
+  wait_selftest_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream_)>>>(d->status, limit_cycles);
+  return check_launch("wait_selftest_kernel");
+}
+
+extern "C" const char* nvfp4_status_string(int s) {
+  switch (s) {
+    case NVFP4_OK: return "ok";
+    case NVFP4_ERR_INVALID_ARG: return "invalid argument";
+    case NVFP4_ERR_SHAPE: return "unsupported shape";
+    case NVFP4_ERR_ALIGNMENT: return "misaligned pointer";
+    case NVFP4_ERR_CUDA: return "CUDA error";
+    case NVFP4_ERR_DEVICE: return "unsupported device";
+    case NVFP4_ERR_TIMEOUT: return "device wait timed out";
+    default: return "unknown status";
+  }
+}
+
+extern "C" const char* nvfp4_last_error(void) { return t_last_error; }
+
+extern "C" int nvfp4_version(void) { return 100; }

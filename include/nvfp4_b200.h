@@ -1,0 +1,84 @@
+/*
+ * nvfp4_b200.h - C ABI of libnvfp4_b200.so, the B200 (sm_100a) kernels for the
+ * two NVFP4 hot paths of kazim05/Blackwell-nvfp4-kernels.
+ *
+ * Plain pointers and sizes only (no torch or CUDA types): `stream` is a
+ * cudaStream_t passed as void* (NULL = legacy default stream).  Every entry
+ * point returns NVFP4_OK (0) or a negative status; no exception crosses the
+ * ABI.  Launches are asynchronous on `stream`; device-side wait timeouts are
+ * reported through nvfp4_device_status().
+ *
+ * Data layouts are those of the reference task (nvfp4_dual_gemm/reference.py,
+ * nvfp4_group_gemm/reference.py):
+ *   A  [M, K/2, L]  float4_e2m1fn_x2, K-major; batch l starts at l*M*K/2 bytes
+ *   B  [N, K/2, L]  same
+ *   SF permuted scale tensor [32, 4, ceil(MN/128), 4, K/64, L] float8_e4m3fn,
+ *      i.e. contiguous 512-byte atoms [L][ceil(MN/128)][K/64][32][4][4]
+ *   C  [M, N, L]    float16, row-major; batch l starts at l*M*N elements
+ * Requirements: K % 256 == 0, N % 8 == 0, M >= 1, all pointers 16-byte aligned.
+ */
+#ifndef NVFP4_B200_H
+#define NVFP4_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define NVFP4_OK 0
+#define NVFP4_ERR_INVALID_ARG (-1)   /* null pointer, negative size, bad count */
+#define NVFP4_ERR_SHAPE (-2)         /* K % 256 != 0, N % 8 != 0, too large */
+#define NVFP4_ERR_ALIGNMENT (-3)     /* a pointer is not 16-byte aligned */
+#define NVFP4_ERR_CUDA (-4)          /* a CUDA runtime / driver call failed */
+#define NVFP4_ERR_DEVICE (-5)        /* current device is not sm_100 */
+#define NVFP4_ERR_TIMEOUT (-6)       /* a kernel's bounded wait ran out */
+
+/* One problem of a grouped GEMM (one entry of the reference's
+ * abc_list / sfasfb_reordered_list / problem_sizes). */
+typedef struct nvfp4_group {
+  const void* a;        /* [M, K/2, L] e2m1 x2 */
+  const void* b;        /* [N, K/2, L] e2m1 x2 */
+  const void* sfa_perm; /* permuted scales of A */
+  const void* sfb_perm; /* permuted scales of B */
+  void* c;              /* [M, N, L] fp16 */
+  int32_t m, n, k, l;
+} nvfp4_group;
+
+/* C = silu(A . B1ᵀ) * (A . B2ᵀ), fp32 accumulation, fp16 output.
+ * Replaces the host launcher torch.ops.<ns>.dual_gemm(A,B1,B2,SFA,SFB1,SFB2,C)
+ * (nvfp4_dual_gemm/submission_v1.py:1305-1356) and the compiled CuTe call of
+ * nvfp4_dual_gemm/submission_v4.py:1256-1284. */
+int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, const void* sfa_perm,
+                    const void* sfb1_perm, const void* sfb2_perm, void* c, int m, int n, int k,
+                    int l, void* stream);
+
+/* C_g = A_g . B_gᵀ for g in [0, num_groups) in one persistent launch (the host
+ * splits tables larger than one launch's parameter block).  Groups with
+ * M == 0 are skipped.  Replaces module.kernel_launch(As,Bs,SFAs,SFBs,Cs,
+ * problem_sizes) (nvfp4_group_gemm/submission_v7.py:454-522). */
+int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream);
+
+/* Synchronises `stream`, then reads and clears this device's status word.
+ * Returns NVFP4_ERR_TIMEOUT if a kernel gave up on a wait (bits in *bits_out,
+ * may be NULL), NVFP4_ERR_CUDA on a CUDA error, else NVFP4_OK.  No reference
+ * counterpart: the reference kernels spin forever. */
+int nvfp4_device_status(void* stream, unsigned* bits_out);
+
+/* Launches a one-CTA kernel that waits on an mbarrier nothing ever completes,
+ * bounded by `limit_cycles`; nvfp4_device_status() must then report
+ * NVFP4_ERR_TIMEOUT.  Exercises the bounded-wait path without faulting.
+ * No reference counterpart. */
+int nvfp4_wait_selftest(long long limit_cycles, void* stream);
+
+/* Status code -> static string.  Detail of the calling thread's last failure. */
+const char* nvfp4_status_string(int status);
+const char* nvfp4_last_error(void);
+
+/* Library version: major*10000 + minor*100 + patch. */
+int nvfp4_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* NVFP4_B200_H */

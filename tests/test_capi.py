@@ -1,0 +1,101 @@
+"""CPU: the C-ABI library loads, exports every symbol include/nvfp4_b200.h
+declares, and rejects bad arguments before touching a GPU; the Python
+drop-ins validate the reference tuples."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from nvfp4_b200 import _lib
+from nvfp4_b200 import build as B
+from nvfp4_b200 import dual_gemm as D
+from nvfp4_b200 import group_gemm as G
+from nvfp4_b200 import inputs as I
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "nvfp4_b200.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    B.build()
+    return _lib.load()
+
+
+def header_functions():
+    text = HEADER.read_text()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(nvfp4_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_what_python_binds():
+    assert header_functions() == sorted(_lib.EXPORTED)
+
+
+def test_library_exports_every_header_symbol(lib):
+    for name in header_functions():
+        assert hasattr(lib, name), name
+
+
+def test_version_and_status_strings(lib):
+    assert lib.nvfp4_version() >= 100
+    assert lib.nvfp4_status_string(0) == b"ok"
+    assert lib.nvfp4_status_string(_lib.NVFP4_ERR_TIMEOUT) == b"device wait timed out"
+    assert lib.nvfp4_status_string(-99) == b"unknown status"
+
+
+def test_no_tma_multicast_in_sources():
+    for p in (ROOT / "blackwell-nvfp4-kernels_b200" / "csrc").glob("*"):
+        assert "multicast::cluster" not in p.read_text().replace(
+            "mbarrier::arrive::one.shared::cluster", ""), p
+
+
+def test_dual_rejects_bad_arguments_without_gpu(lib):
+    p = ctypes.c_void_p(4096)   # never dereferenced: validation fails first
+    f = lib.nvfp4_dual_gemm
+    assert f(None, p, p, p, p, p, p, 128, 128, 256, 1, None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert f(p, p, p, p, p, p, p, 0, 128, 256, 1, None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert f(p, p, p, p, p, p, p, 128, 128, 320, 1, None) == _lib.NVFP4_ERR_SHAPE
+    assert b"256" in lib.nvfp4_last_error()
+    assert f(p, p, p, p, p, p, p, 128, 100, 256, 1, None) == _lib.NVFP4_ERR_SHAPE
+    q = ctypes.c_void_p(4096 + 8)
+    assert f(p, q, p, p, p, p, p, 128, 128, 256, 1, None) == _lib.NVFP4_ERR_ALIGNMENT
+
+
+def test_grouped_rejects_bad_arguments_without_gpu(lib):
+    t = (_lib.Group * 2)()
+    t[0] = _lib.Group(4096, 4096, 4096, 4096, 4096, 128, 128, 256, 1)
+    t[1] = _lib.Group(4096, 4096, 4096, 4096, 4096, 128, 128, 300, 1)
+    assert lib.nvfp4_grouped_gemm(t, 2, None) == _lib.NVFP4_ERR_SHAPE
+    t[1] = _lib.Group(None, 4096, 4096, 4096, 4096, 64, 128, 256, 1)
+    assert lib.nvfp4_grouped_gemm(t, 2, None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert lib.nvfp4_grouped_gemm(None, 1, None) == _lib.NVFP4_ERR_INVALID_ARG
+    # only empty groups: nothing to launch
+    t[0] = _lib.Group(None, None, None, None, None, 0, 128, 256, 1)
+    assert lib.nvfp4_grouped_gemm(t, 1, None) == _lib.NVFP4_OK
+
+
+def test_check_raises_with_detail(lib):
+    p = ctypes.c_void_p(4096)
+    st = lib.nvfp4_dual_gemm(p, p, p, p, p, p, p, 128, 128, 320, 1, None)
+    with pytest.raises(_lib.Nvfp4Error, match="multiple of 256"):
+        _lib.check(st)
+
+
+def test_python_dropin_validates_tuples():
+    d = I.generate_dual_input(256, 128, 256, 1, seed=1, device="cpu")
+    with pytest.raises(ValueError, match="CUDA"):
+        D.custom_kernel(d)
+    g = I.generate_group_input([64], [128], [256], 1, seed=1, device="cpu")
+    with pytest.raises(ValueError, match="CUDA"):
+        G.custom_kernel(g)
+
+
+def test_sf_layout_validation():
+    d = I.generate_dual_input(256, 128, 256, 1, seed=1, device="cpu")
+    pa = d[6]
+    D.check_sf_perm("sfa", pa, 256, 256, 1, pa.device)
+    bad = pa.contiguous()   # logical-order contiguous: not the atom memory image
+    with pytest.raises(ValueError, match="strides"):
+        D.check_sf_perm("sfa", bad, 256, 256, 1, bad.device)

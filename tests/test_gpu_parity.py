@@ -1,0 +1,243 @@
+"""GPU parity: the CUDA kernels (through the C ABI via the drop-in
+``custom_kernel``s) against the CPU oracle on the same seeded inputs, at the
+reference's task shapes (nvfp4_dual_gemm/task.yml:46-56,
+nvfp4_group_gemm/task.yml:47-57), the benchmark configurations, and edge
+cases.  Tolerance: rtol = atol = 1e-2 on fp16 outputs (fp32 accumulation),
+NaN/inf-aware as in nvfp4_group_gemm/utils.py:31-86."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from nvfp4_b200 import _lib
+from nvfp4_b200 import build as B
+from nvfp4_b200 import dual_gemm as D
+from nvfp4_b200 import group_gemm as G
+from nvfp4_b200 import inputs as I
+from oracle import nvfp4_oracle as O
+
+pytestmark = pytest.mark.gpu
+RTOL = ATOL = 1e-2
+
+DUAL_TASK_TESTS = [  # nvfp4_dual_gemm/task.yml:46-56 (m, n, k, l)
+    (1536, 512, 7168, 1), (256, 512, 256, 1), (3072, 1024, 1536, 1), (7168, 1024, 256, 1),
+    (7168, 2304, 2048, 1), (4608, 384, 7168, 1), (7168, 384, 2304, 1), (512, 768, 7168, 1),
+    (4096, 768, 512, 1),
+]
+DUAL_TASK_BENCH = [(256, 4096, 7168, 1), (512, 4096, 7168, 1), (256, 3072, 4096, 1),
+                   (512, 3072, 7168, 1)]  # nvfp4_dual_gemm/task.yml:58-62
+GROUP_TASK_TESTS = [  # nvfp4_group_gemm/task.yml:47-57
+    ([96, 128], [128, 256], [256, 512]), ([256, 72], [512, 384], [256, 256]),
+    ([128, 128], [128, 256], [512, 256]), ([80, 128, 256], [384, 256, 128], [256, 512, 256]),
+    ([64, 72, 96], [128, 384, 512], [512, 512, 256]), ([64, 256, 128], [768, 128, 256], [512, 256, 512]),
+    ([128, 128, 64], [256, 512, 512], [768, 256, 768]),
+    ([128] * 4, [128] * 4, [512, 256, 512, 256]), ([40, 56, 384, 512], [512, 384, 256, 128], [256] * 4),
+    ([512, 384, 256, 128], [256] * 4, [512, 768, 512, 768]),
+]
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _lib_ready(cuda_device):
+    B.build()
+    _lib.load()
+    assert _lib.device_status() == 0
+
+
+def _np(t):
+    return t.detach().cpu().view(torch.uint8).numpy() if t.dtype != torch.float16 \
+        else t.detach().cpu().numpy()
+
+
+def oracle_dual(data):
+    a, b1, b2, sfa, sfb1, sfb2 = (_np(t) for t in data[:6])
+    return O.ref_dual_batched(a, b1, b2, sfa, sfb1, sfb2)
+
+
+def oracle_group(data):
+    abc, sfab, _, _ = data
+    return O.ref_grouped([(_np(a), _np(b), _np(sa), _np(sb)) for (a, b, _), (sa, sb) in zip(abc, sfab)])
+
+
+def assert_close(got, want, what):
+    bad, idx = O.allclose_report(got, want, RTOL, ATOL)
+    if bad:
+        i = tuple(idx[0])
+        pytest.fail(f"{what}: {bad} mismatches of {want.size}; first {i}: got {got[i]} want {want[i]}")
+
+
+def run_dual(data):
+    out = D.custom_kernel(data)
+    assert _lib.device_status() == 0
+    return out.cpu().numpy()
+
+
+@pytest.mark.parametrize("m,n,k,l", DUAL_TASK_TESTS)
+def test_dual_task_shapes(m, n, k, l):
+    data = I.generate_dual_input(m, n, k, l, seed=1111, device="cuda")
+    assert_close(run_dual(data), oracle_dual(data), f"dual {m}x{n}x{k}")
+
+
+@pytest.mark.parametrize("bn", ["64", "128"])
+@pytest.mark.parametrize("m,n,k,l", DUAL_TASK_BENCH + [(200, 264, 512, 1), (384, 640, 1024, 2)])
+def test_dual_both_tile_widths(m, n, k, l, bn, monkeypatch):
+    monkeypatch.setenv("NVFP4_DUAL_BN", bn)
+    data = I.generate_dual_input(m, n, k, l, seed=42 + m, device="cuda")
+    assert_close(run_dual(data), oracle_dual(data), f"dual bn={bn} {m}x{n}x{k}x{l}")
+
+
+def test_dual_config0_normal_inputs():
+    data = I.dual_config_input(0, device="cuda")
+    assert_close(run_dual(data), oracle_dual(data), "dual config 0")
+
+
+def test_dual_small_m_and_ragged():
+    for (m, n, k) in [(1, 8, 256), (7, 136, 256), (130, 72, 768), (128, 7168, 2048)]:
+        data = I.generate_dual_input(m, n, k, 1, seed=m + n, device="cuda")
+        assert_close(run_dual(data), oracle_dual(data), f"dual {m}x{n}x{k}")
+
+
+def test_dual_deterministic():
+    data = I.generate_dual_input(512, 1024, 2048, 1, seed=3, device="cuda")
+    r1 = D.custom_kernel(data).clone()
+    r2 = D.custom_kernel(data).clone()
+    assert torch.equal(r1, r2)
+
+
+def _rows(t, rows):
+    """Row subset of a packed/scale tensor (index a uint8 view: CUDA indexing
+    is not implemented for the fp4 dtype)."""
+    return t.view(torch.uint8)[rows.to(t.device)]
+
+
+def _sample_rows_check(data, rows):
+    a, b1, b2, sfa, sfb1, sfb2 = data[:6]
+    sub = lambda t: _np(_rows(t, rows))[:, :, 0]
+    want = O.ref_dual(sub(a), _np(b1)[:, :, 0], _np(b2)[:, :, 0], sub(sfa),
+                      _np(sfb1)[:, :, 0], _np(sfb2)[:, :, 0])
+    return want
+
+
+@pytest.mark.parametrize("cfg", [1, 2])
+def test_dual_full_size_configs_sampled_rows(cfg):
+    """Full BASELINE sizes: every row of a seeded sample of 96 rows (all
+    columns) against the oracle, and no NaN anywhere in the output."""
+    data = I.dual_config_input(cfg, device="cuda")
+    out = D.custom_kernel(data)
+    assert _lib.device_status() == 0
+    m = out.shape[0]
+    g = torch.Generator().manual_seed(cfg)
+    rows = torch.randperm(m, generator=g)[:96].sort().values
+    want = _sample_rows_check(data, rows)
+    assert_close(out[rows.to(out.device), :, 0].cpu().numpy(), want, f"dual cfg{cfg} sampled rows")
+    # fp16 overflow to +-inf is legitimate at large K (the oracle agrees on
+    # the sampled rows); NaN never is
+    assert not torch.isnan(out).any()
+
+
+@pytest.mark.parametrize("case", range(len(GROUP_TASK_TESTS)))
+def test_group_task_shapes(case):
+    m, n, k = GROUP_TASK_TESTS[case]
+    data = I.generate_group_input(m, n, k, len(m), seed=1111, device="cuda")
+    outs = G.custom_kernel(data)
+    assert _lib.device_status() == 0
+    for i, (got, want) in enumerate(zip(outs, oracle_group(data))):
+        assert_close(got.cpu().numpy(), want, f"group case {case} g{i}")
+
+
+def test_group_zero_and_many_groups():
+    # a zero-M group, ragged M, and more groups than one 16-entry launch holds
+    ms = [0, 64, 40, 0, 200, 128] + [8 * (i + 1) for i in range(14)]
+    g = len(ms)
+    gen = torch.Generator().manual_seed(77)
+    pairs = [(torch.randn(mi, 512, generator=gen), torch.randn(256, 512, generator=gen)) for mi in ms]
+    data = I.group_from_fp32(pairs, device="cuda")
+    outs = G.custom_kernel(data)
+    assert _lib.device_status() == 0
+    for i, (got, want) in enumerate(zip(outs, oracle_group(data))):
+        assert_close(got.cpu().numpy(), want, f"group g{i} (m={ms[i]})")
+    assert g > 16
+
+
+def test_group_more_than_one_launch():
+    ms = [16 * (i % 7 + 1) for i in range(100)]   # > 96 groups: two launches
+    gen = torch.Generator().manual_seed(5)
+    pairs = [(torch.randn(mi, 256, generator=gen), torch.randn(128, 256, generator=gen)) for mi in ms]
+    data = I.group_from_fp32(pairs, device="cuda")
+    outs = G.custom_kernel(data)
+    assert _lib.device_status() == 0
+    for i, (got, want) in enumerate(zip(outs, oracle_group(data))):
+        assert_close(got.cpu().numpy(), want, f"group g{i}")
+
+
+def test_group_config3_full_size():
+    data = I.group_config_input(3, device="cuda")
+    outs = G.custom_kernel(data)
+    assert _lib.device_status() == 0
+    # full check of the two smallest groups, sampled rows elsewhere
+    abc, sfab, _, sizes = data
+    order = sorted(range(len(sizes)), key=lambda i: sizes[i][0])
+    for i in order[:2]:
+        (a, b, _), (sa, sb) = abc[i], sfab[i]
+        want = O.ref_group(_np(a)[:, :, 0], _np(b)[:, :, 0], _np(sa)[:, :, 0], _np(sb)[:, :, 0])
+        assert_close(outs[i][:, :, 0].cpu().numpy(), want, f"cfg3 group {i}")
+    for i in order[2:]:
+        (a, b, _), (sa, sb) = abc[i], sfab[i]
+        rows = torch.arange(0, sizes[i][0], 97)
+        want = O.ref_group(_np(_rows(a, rows))[:, :, 0], _np(b)[:, :, 0],
+                           _np(_rows(sa, rows))[:, :, 0], _np(sb)[:, :, 0])
+        assert_close(outs[i][rows.to(outs[i].device), :, 0].cpu().numpy(), want,
+                     f"cfg3 group {i} sampled")
+
+
+def test_group_config4_sampled():
+    data = I.group_config_input(4, device="cuda")
+    outs = G.custom_kernel(data)
+    assert _lib.device_status() == 0
+    abc, sfab, _, sizes = data
+    assert any(s[0] == 0 for s in sizes) or min(s[0] for s in sizes) < 128
+    for i in range(0, len(sizes), 9):
+        if sizes[i][0] == 0:
+            continue
+        (a, b, _), (sa, sb) = abc[i], sfab[i]
+        rows = torch.arange(0, sizes[i][0], max(1, sizes[i][0] // 16))
+        want = O.ref_group(_np(_rows(a, rows))[:, :, 0], _np(b)[:, :, 0],
+                           _np(_rows(sa, rows))[:, :, 0], _np(sb)[:, :, 0])
+        assert_close(outs[i][rows.to(outs[i].device), :, 0].cpu().numpy(), want, f"cfg4 expert {i}")
+
+
+def test_oracle_matches_scaled_mm_live():
+    """Pin the oracle (nibble order, scale layout, fp32 accumulation) against
+    torch._scaled_mm called as nvfp4_dual_gemm/reference.py:56-73 does."""
+    from nvfp4_b200.formats import to_blocked
+    for (m, n, k) in [(128, 128, 256), (256, 384, 1024), (72, 144, 512)]:
+        data = I.generate_dual_input(m, n, k, 1, seed=m * 7 + k, device="cuda")
+        a, b1, _, sfa, sfb1 = data[0], data[1], data[2], data[3], data[4]
+        r1 = torch._scaled_mm(a[:, :, 0], b1[:, :, 0].transpose(0, 1),
+                              to_blocked(sfa[:, :, 0]).cuda(), to_blocked(sfb1[:, :, 0]).cuda(),
+                              bias=None, out_dtype=torch.float32)
+        ours = O.scaled_mm_f32(_np(a)[:, :, 0], _np(sfa)[:, :, 0], _np(b1)[:, :, 0], _np(sfb1)[:, :, 0])
+        np.testing.assert_allclose(ours, r1.cpu().numpy(), rtol=1e-5, atol=1e-3)
+
+
+def test_wait_timeout_reports_status():
+    """A bounded wait on an mbarrier nothing completes ends with a status,
+    not a hang; the context stays usable afterwards."""
+    lib = _lib.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.nvfp4_wait_selftest(2_000_000, stream))
+    bits = _lib.device_status(stream)
+    assert bits != 0
+    assert _lib.device_status(stream) == 0           # cleared
+    data = I.generate_dual_input(256, 256, 256, 1, seed=9, device="cuda")
+    assert_close(run_dual(data), oracle_dual(data), "dual after timeout self-test")
+
+
+def test_device_quantisation_bit_exact():
+    """formats.quantize_nvfp4 on the GPU == the oracle (bit-exact)."""
+    from nvfp4_b200.formats import quantize_nvfp4
+    g = torch.Generator().manual_seed(123)
+    x = torch.randn(512, 1024, generator=g) * 3
+    p, s = quantize_nvfp4(x.cuda())
+    po, so = O.quantize_nvfp4(x.numpy())
+    assert np.array_equal(s.cpu().numpy(), so) and np.array_equal(p.cpu().numpy(), po)
