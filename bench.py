@@ -281,6 +281,8 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="device-timed calls only (no e2e, no CPU baseline): the profiling run")
     args = ap.parse_args()
     assert args.warmup >= 3 or args.impl == "reference", "need >= 3 warm-up steps"
 
@@ -317,12 +319,14 @@ def main():
         pg.barrier()
     torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        torch.cuda.nvtx.range_push("timed")
         for i in range(args.steps):
             flush.zero_()                       # evict L2 between calls (outside the events)
             starts[i].record(stream)
             call(cfg, data)
             ends[i].record(stream)
         torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
     if pg:
         pg.barrier()
     status = _lib.device_status()
@@ -337,6 +341,15 @@ def main():
     total_flop = flop_t.item() * args.steps
     value = total_flop / t_max_s / 1e12
     ms_per_step = t_max_s * 1e3 / args.steps
+
+    if args.kernel_only:
+        if rank == 0:
+            print(json.dumps({"metric": metric_name(cfg), "value": round(value, 2),
+                              "unit": "TFLOP/s", "us_per_call": round(ms_per_step * 1e3, 2),
+                              "config": desc, "kernel_only": True}), flush=True)
+        if pg:
+            pg.destroy_process_group()
+        return
 
     # ---- e2e through the public API with pinned host buffers
     ins, outs = device_tensors(cfg, data)

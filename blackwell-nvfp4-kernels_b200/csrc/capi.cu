@@ -10,6 +10,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 #include <vector>
 
 #include "../../include/nvfp4_b200.h"
@@ -52,7 +53,7 @@ struct DeviceState {
   bool ready = false;
   int num_sms = 0;
   unsigned* status = nullptr;
-  bool smem_set[16] = {};
+  bool smem_set[16] = {};  // one slot per kernel instantiation
 };
 
 std::mutex g_mu;
@@ -114,7 +115,8 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // 3-D byte view [L][rows][K/2] of a packed e2m1 operand, box {128 B, box_rows, 1},
 // 128-byte swizzle (the canonical K-major SW128 operand layout of tcgen05.mma).
-int encode_operand(CUtensorMap* map, const void* base, int rows, int k, int l, int box_rows) {
+int encode_operand_uncached(CUtensorMap* map, const void* base, int rows, int k, int l,
+                            int box_rows) {
   const cuuint64_t dims[3] = {(cuuint64_t)(k / 2), (cuuint64_t)rows, (cuuint64_t)l};
   const cuuint64_t strides[2] = {(cuuint64_t)(k / 2), (cuuint64_t)rows * (cuuint64_t)(k / 2)};
   const cuuint32_t box[3] = {128u, (cuuint32_t)box_rows, 1u};
@@ -126,6 +128,46 @@ int encode_operand(CUtensorMap* map, const void* base, int rows, int k, int l, i
   if (r != CUDA_SUCCESS)
     return fail(NVFP4_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) rows=%d k=%d l=%d", (int)r,
                 rows, k, l);
+  return NVFP4_OK;
+}
+
+// Encoded descriptors are pure functions of (address, rows, K, L, box rows);
+// repeated calls on the same tensors (the common case: weights, persistent
+// activation buffers) reuse them instead of re-encoding.
+struct MapKey {
+  uintptr_t ptr;
+  int rows, k, l, box;
+  bool operator==(const MapKey& o) const {
+    return ptr == o.ptr && rows == o.rows && k == o.k && l == o.l && box == o.box;
+  }
+};
+struct MapKeyHash {
+  size_t operator()(const MapKey& key) const {
+    uint64_t h = key.ptr * 0x9E3779B97F4A7C15ull;
+    h ^= ((uint64_t)(uint32_t)key.rows << 32 | (uint32_t)key.k) + 0x632BE59BD9B4E019ull + (h << 6);
+    h ^= ((uint64_t)(uint32_t)key.l << 32 | (uint32_t)key.box) + (h >> 2);
+    return (size_t)h;
+  }
+};
+std::mutex g_map_mu;
+std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
+constexpr size_t kMaxCachedMaps = 8192;
+
+int encode_operand(CUtensorMap* map, const void* base, int rows, int k, int l, int box_rows) {
+  const MapKey key{reinterpret_cast<uintptr_t>(base), rows, k, l, box_rows};
+  {
+    std::lock_guard<std::mutex> lk(g_map_mu);
+    auto it = g_maps.find(key);
+    if (it != g_maps.end()) {
+      *map = it->second;
+      return NVFP4_OK;
+    }
+  }
+  int rc = encode_operand_uncached(map, base, rows, k, l, box_rows);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(g_map_mu);
+  if (g_maps.size() >= kMaxCachedMaps) g_maps.clear();
+  g_maps.emplace(key, *map);
   return NVFP4_OK;
 }
 
@@ -160,13 +202,12 @@ int launch_dual(DeviceState* d, int slot, DualParams& p, cudaStream_t stream) {
 }
 
 // ---------------------------------------------------------------- grouped GEMM
-template <int kMaxGroups>
-int launch_grouped_chunk(DeviceState* d, const nvfp4_group* gs, const int* idx, int count,
+template <int kBN, int kStages, int kEpiWarps, int kAccBufs, int kMaxGroups>
+int launch_grouped_chunk(DeviceState* d, int slot, const nvfp4_group* gs, const int* idx, int count,
                          cudaStream_t stream) {
-  constexpr int kBN = 128, kStages = 6;
-  using Cfg = GroupedCfg<kBN, kStages>;
-  auto kern = grouped_gemm_kernel<kBN, kStages, kMaxGroups>;
-  int rc = set_smem_once(d, kMaxGroups == 16 ? 8 : 9, kern, Cfg::kSmemBytes);
+  using Cfg = GroupedCfg<kBN, kStages, kEpiWarps, kAccBufs>;
+  auto kern = grouped_gemm_kernel<kBN, kStages, kEpiWarps, kAccBufs, kMaxGroups>;
+  int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
   if (rc) return rc;
   static thread_local GroupedParams<kMaxGroups> p;
   int tiles = 0;
@@ -192,6 +233,17 @@ int launch_grouped_chunk(DeviceState* d, const nvfp4_group* gs, const int* idx, 
   const int grid = tiles < d->num_sms ? tiles : d->num_sms;
   kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   return check_launch("grouped_gemm_kernel");
+}
+
+// 128x256 tiles (4 stages, 8 epilogue warps, one accumulator buffer) when
+// every group is at least 256 wide, else 128x128 tiles (6 stages, 4 epilogue
+// warps, two accumulator buffers).
+template <int kMaxGroups>
+int launch_grouped(DeviceState* d, const nvfp4_group* gs, const int* idx, int count, int bn,
+                   cudaStream_t stream) {
+  const int base = kMaxGroups == 16 ? 4 : 6;
+  if (bn == 256) return launch_grouped_chunk<256, 4, 8, 1, kMaxGroups>(d, base, gs, idx, count, stream);
+  return launch_grouped_chunk<128, 6, 4, 2, kMaxGroups>(d, base + 1, gs, idx, count, stream);
 }
 
 }  // namespace
@@ -272,10 +324,15 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
   if (rc) return rc;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const int n = (int)live.size();
-  if (n <= 16) return launch_grouped_chunk<16>(d, groups, live.data(), n, stream);
+  int min_n = groups[live[0]].n;
+  for (int i : live) min_n = groups[i].n < min_n ? groups[i].n : min_n;
+  int bn = min_n >= 256 ? 256 : 128;
+  const int forced = env_int("NVFP4_GROUPED_BN", 0);
+  if (forced == 128 || forced == 256) bn = forced;
+  if (n <= 16) return launch_grouped<16>(d, groups, live.data(), n, bn, stream);
   for (int s = 0; s < n; s += 96) {
     const int cnt = n - s < 96 ? n - s : 96;
-    if ((rc = launch_grouped_chunk<96>(d, groups, live.data() + s, cnt, stream))) return rc;
+    if ((rc = launch_grouped<96>(d, groups, live.data() + s, cnt, bn, stream))) return rc;
   }
   return NVFP4_OK;
 }

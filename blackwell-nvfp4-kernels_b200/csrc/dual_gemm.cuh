@@ -13,13 +13,14 @@
 //   kEpiWarps issues TMA (A, B1, B2 tiles with 128-byte swizzle, scale atoms
 //   with bulk copies), warp kEpiWarps+1 owns TMEM and issues tcgen05.cp +
 //   tcgen05.mma;
-// * one A stage feeds two MMAs per K step: the gate MMA loads A into the
-//   tensor core's collector, the up MMA reuses it (collector::a::fill /
-//   lastuse), so A is read from shared memory once;
+// * B1 and B2 tiles sit back to back in shared memory, so for 128-wide tiles
+//   one tcgen05.mma with N = 256 computes gate and up together from a single
+//   read of the A tile (accumulator columns [0,128) = gate, [128,256) = up);
+//   64-wide tiles issue two N=64 MMAs;
 // * scale factors go shared -> TMEM with tcgen05.cp (one 512-byte atom per
-//   64-K step per operand) into one TMEM region per stage; tcgen05.cp and
-//   tcgen05.mma issued by one thread execute in order, so the region is
-//   reused stage after stage;
+//   64-K step per operand); the scale region is double-buffered across
+//   stages, so copying the next stage's scales never has to wait for the
+//   MMAs still reading the current ones;
 // * kAccBufs accumulator sets (gate + up, kBN columns each) in TMEM; with one
 //   set the epilogue loads all of its columns to registers and releases TMEM
 //   before doing the math and stores, so the next tile's MMAs start early.
@@ -54,10 +55,12 @@ struct DualCfg {
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024;  // + alignment slack
   static constexpr int kTmemCols = 512;
   static constexpr int kAccCols = 2 * kBN;            // gate + up
-  static constexpr int kSfCol = kAccBufs * kAccCols;  // TMEM column of the scale region
+  static constexpr int kSfCol = kAccBufs * kAccCols;  // TMEM column of the scale regions
+  static constexpr int kSfBufCols = 48;               // per buffer: SFA 4x4 + SFB 4x8 columns
   static constexpr int kColsPerWarp = kBN / (kEpiWarps / 4);
   static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned");
-  static_assert(kSfCol + 48 <= kTmemCols, "TMEM budget");
+  static_assert(kSfCol + 2 * kSfBufCols <= kTmemCols, "TMEM budget");
+  static_assert(kSfCol % 4 == 0 && kSfBufCols % 4 == 0, "tcgen05.cp needs 4-column alignment");
   static_assert(kEpiWarps % 4 == 0, "epilogue warps cover all four TMEM lane quadrants");
   static_assert(kColsPerWarp % 32 == 0, "epilogue loads 32 columns at a time");
   static_assert(kBN == 64 || kBN == 128, "tile N");
@@ -176,26 +179,25 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
   } else if (warp == kEpiWarps + 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_mxf4nvf4<kBM, kBN>();
-      const uint32_t sf_a = tmem + Cfg::kSfCol;
-      const uint32_t sf_b1 = sf_a + 16;
-      const uint32_t sf_b2 = sf_a + 32;
+      // 128-wide tiles: one M=128, N=256 MMA per 64-K step over [B1 tile ; B2 tile];
+      // 64-wide tiles: two N=64 MMAs (gate, up)
+      constexpr uint32_t idesc = idesc_mxf4nvf4<kBM, kBN == 128 ? 2 * kBN : kBN>();
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      uint32_t sf_buf = 0;
       bool ok = true, any = false;
       for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
         const TileCoord tc = dual_tile_coord(p, t);
-        // scale columns of this tile's 64/128 B rows inside the 128-row atom
-        const uint32_t sfb_sub = (kBN == 64) ? (uint32_t)((tc.nb & 1) * 2) : 0u;
+        // 64-wide tiles use half of each 128-row scale atom: columns {0,1} or {2,3}
+        const uint32_t sub = (kBN == 64) ? (uint32_t)((tc.nb & 1) * 2) : 0u;
         if (!ctl.wait(smem_u32(&bar_acc_empty[acc]), acc_phase ^ 1u, kDevTimeoutAccFree)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t d_gate = tmem + acc * Cfg::kAccCols;
-        const uint32_t d_up = d_gate + kBN;
+        const uint32_t d_acc = tmem + acc * Cfg::kAccCols;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!ctl.wait(smem_u32(&bar_full[stage]), phase, kDevTimeoutTmaFull)) {
             ok = false;
@@ -203,31 +205,38 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
           }
           tc_fence_after();
           const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
-          const uint32_t sb1 = sa + Cfg::kABytes;
-          const uint32_t sb2 = sb1 + Cfg::kBBytes;
-          const uint32_t ssf = sb2 + Cfg::kBBytes;
+          const uint32_t sb = sa + Cfg::kABytes;             // B1 rows then B2 rows
+          const uint32_t ssf = sb + 2 * Cfg::kBBytes;
+          const uint32_t sf_a = tmem + Cfg::kSfCol + sf_buf * Cfg::kSfBufCols;
+          const uint32_t sf_b = sf_a + 16;
+          // scale atoms for k-step j: SFA -> [sf_a+4j, +4), SFB1 | SFB2 -> [sf_b+8j, +8)
+          // (tcgen05.cp destinations stay 4-column aligned)
           #pragma unroll
           for (int j = 0; j < kBK / kKStep; ++j) {
             tc_cp_sf_atom(sf_a + 4 * j, sf_atom_desc(ssf + j * kSfAtom));
-            tc_cp_sf_atom(sf_b1 + 4 * j, sf_atom_desc(ssf + kSfStageBytes + j * kSfAtom));
-            tc_cp_sf_atom(sf_b2 + 4 * j, sf_atom_desc(ssf + 2 * kSfStageBytes + j * kSfAtom));
+            tc_cp_sf_atom(sf_b + 8 * j, sf_atom_desc(ssf + kSfStageBytes + j * kSfAtom));
+            tc_cp_sf_atom(sf_b + 8 * j + 4, sf_atom_desc(ssf + 2 * kSfStageBytes + j * kSfAtom));
           }
           #pragma unroll
           for (int j = 0; j < kBK / kKStep; ++j) {
             const uint64_t da = kmajor_sw128_desc(sa + 32 * j);
-            const uint64_t db1 = kmajor_sw128_desc(sb1 + 32 * j);
-            const uint64_t db2 = kmajor_sw128_desc(sb2 + 32 * j);
             const uint32_t accum = (kb | j) != 0;
-#if NVFP4_DUAL_A_COLLECTOR
-            tc_mma_nvf4_a_fill(d_gate, da, db1, idesc, sf_a + 4 * j, sf_b1 + 4 * j + sfb_sub, accum);
-            tc_mma_nvf4_a_lastuse(d_up, da, db2, idesc, sf_a + 4 * j, sf_b2 + 4 * j + sfb_sub, accum);
-#else
-            tc_mma_nvf4(d_gate, da, db1, idesc, sf_a + 4 * j, sf_b1 + 4 * j + sfb_sub, accum);
-            tc_mma_nvf4(d_up, da, db2, idesc, sf_a + 4 * j, sf_b2 + 4 * j + sfb_sub, accum);
-#endif
+            if constexpr (kBN == 128) {
+              // one N=256 MMA over [B1 ; B2]: the 8 scale columns are exactly
+              // SFB1 rows 0..127 then SFB2 rows 0..127
+              tc_mma_nvf4(d_acc, da, kmajor_sw128_desc(sb + 32 * j), idesc, sf_a + 4 * j,
+                          sf_b + 8 * j, accum);
+            } else {
+              // 64-row halves of the atoms sit in columns {0,1} or {2,3}: two N=64 MMAs
+              tc_mma_nvf4(d_acc, da, kmajor_sw128_desc(sb + 32 * j), idesc, sf_a + 4 * j,
+                          sf_b + 8 * j + sub, accum);
+              tc_mma_nvf4(d_acc + kBN, da, kmajor_sw128_desc(sb + Cfg::kBBytes + 32 * j), idesc,
+                          sf_a + 4 * j, sf_b + 8 * j + 4 + sub, accum);
+            }
           }
           tc_commit(smem_u32(&bar_empty[stage]));  // frees the stage once these MMAs finish
           any = true;
+          sf_buf ^= 1u;
           if (++stage == kStages) stage = 0, phase ^= 1u;
         }
         if (!ok) break;

@@ -15,8 +15,11 @@
 //   column so a B tile is reused from L2 by all M-blocks of its group); every
 //   CTA walks the list round-robin and finds its group by binary search over
 //   the tile-start prefix sums;
-// * two TMEM accumulator buffers, so the epilogue of one tile overlaps the
-//   MMAs of the next; empty groups are compacted out on the host.
+// * 128x256 tiles (one N=256 MMA per 64-K step, one accumulator buffer whose
+//   columns the epilogue pulls into registers before releasing it) or
+//   128x128 tiles (two accumulator buffers, so the epilogue of one tile
+//   overlaps the MMAs of the next); the scale-factor TMEM region is
+//   double-buffered across stages; empty groups are compacted out on the host.
 #pragma once
 #include <cuda.h>
 #include "kernel_common.cuh"
@@ -41,20 +44,24 @@ struct GroupedParams {
   long long wait_limit;
 };
 
-template <int kBN, int kStages>
+template <int kBN, int kStages, int kEpiWarps, int kAccBufs>
 struct GroupedCfg {
-  static constexpr int kEpiWarps = 4;
-  static constexpr int kAccBufs = 2;
   static constexpr int kABytes = kBM * kBK / 2;
   static constexpr int kBBytes = kBN * kBK / 2;
-  static constexpr int kStageBytes = kABytes + kBBytes + 2 * kSfStageBytes;
+  static constexpr int kSfbAtoms = kBN / 128;                  // 128-row scale atoms per tile
+  static constexpr int kSfbBytes = kSfbAtoms * kSfStageBytes;
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfStageBytes + kSfbBytes;
   static constexpr int kThreads = 32 * (kEpiWarps + 2);
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024;
   static constexpr int kTmemCols = 512;
   static constexpr int kSfCol = kAccBufs * kBN;
+  static constexpr int kSfBufCols = 16 + 16 * kSfbAtoms;       // SFA 4x4 + SFB 4x(4*atoms)
+  static constexpr int kColsPerWarp = kBN / (kEpiWarps / 4);
   static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned");
-  static_assert(kSfCol + 32 <= kTmemCols, "TMEM budget");
-  static_assert(kBN == 128 || kBN == 64, "tile N");
+  static_assert(kSfCol + 2 * kSfBufCols <= kTmemCols, "TMEM budget");
+  static_assert(kSfCol % 4 == 0 && kSfBufCols % 4 == 0, "tcgen05.cp needs 4-column alignment");
+  static_assert(kBN == 128 || kBN == 256, "tile N");
+  static_assert(kEpiWarps % 4 == 0 && kColsPerWarp % 32 == 0, "epilogue split");
 };
 
 struct GTile { int g, l, mb, nb; };
@@ -78,13 +85,13 @@ __device__ __forceinline__ GTile grouped_tile(const GroupedParams<kMaxGroups>& p
   return r;
 }
 
-template <int kBN, int kStages, int kMaxGroups>
-__global__ void __launch_bounds__(GroupedCfg<kBN, kStages>::kThreads, 1)
+template <int kBN, int kStages, int kEpiWarps, int kAccBufs, int kMaxGroups>
+__global__ void __launch_bounds__(GroupedCfg<kBN, kStages, kEpiWarps, kAccBufs>::kThreads, 1)
 grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
-  using Cfg = GroupedCfg<kBN, kStages>;
+  using Cfg = GroupedCfg<kBN, kStages, kEpiWarps, kAccBufs>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_full[kStages], bar_empty[kStages];
-  __shared__ uint64_t bar_acc_full[Cfg::kAccBufs], bar_acc_empty[Cfg::kAccBufs];
+  __shared__ uint64_t bar_acc_full[kAccBufs], bar_acc_empty[kAccBufs];
   __shared__ uint64_t bar_drain;
   __shared__ uint32_t s_tmem_base;
   __shared__ volatile int s_abort;
@@ -92,16 +99,16 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const int warp = threadIdx.x >> 5;
   const uint32_t lane = lane_id();
-  constexpr int kProd = Cfg::kEpiWarps, kMma = Cfg::kEpiWarps + 1;
+  constexpr int kProd = kEpiWarps, kMma = kEpiWarps + 1;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&bar_full[s]), 1);
       mbar_init(smem_u32(&bar_empty[s]), 1);
     }
-    for (int b = 0; b < Cfg::kAccBufs; ++b) {
+    for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(smem_u32(&bar_acc_full[b]), 1);
-      mbar_init(smem_u32(&bar_acc_empty[b]), Cfg::kEpiWarps);
+      mbar_init(smem_u32(&bar_acc_empty[b]), kEpiWarps);
     }
     mbar_init(smem_u32(&bar_drain), 1);
     s_abort = 0;
@@ -137,7 +144,8 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
         const int k_blocks = gi.k / kBK;
         const int rest_k = gi.k / kKStep;
         const size_t sfa_l = (size_t)gi.m_blocks * rest_k * kSfAtom;
-        const size_t sfb_l = (size_t)((gi.n + 127) / 128) * rest_k * kSfAtom;
+        const int n_atoms = (gi.n + 127) / 128;
+        const size_t sfb_l = (size_t)n_atoms * rest_k * kSfAtom;
         const int n0 = tc.nb * kBN;
         const uint8_t* sfa_t = gi.sfa + tc.l * sfa_l + (size_t)tc.mb * rest_k * kSfAtom;
         const uint8_t* sfb_t = gi.sfb + tc.l * sfb_l + (size_t)(n0 / 128) * rest_k * kSfAtom;
@@ -155,7 +163,14 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
           tma_load_3d(sb, &p.tmap_b[tc.g], full, kb * 128, n0, tc.l, pol);
           const size_t sf_off = (size_t)kb * kSfStageBytes;
           bulk_load(ssf, sfa_t + sf_off, kSfStageBytes, full, pol);
-          bulk_load(ssf + kSfStageBytes, sfb_t + sf_off, kSfStageBytes, full, pol);
+          #pragma unroll
+          for (int a = 0; a < Cfg::kSfbAtoms; ++a) {
+            // consecutive 128-row atom blocks; a block past N (rows that are
+            // never stored) re-reads the last real block instead
+            const int blk = min(n0 / 128 + a, n_atoms - 1) - n0 / 128;
+            bulk_load(ssf + (1 + a) * kSfStageBytes,
+                      sfb_t + blk * (size_t)rest_k * kSfAtom + sf_off, kSfStageBytes, full, pol);
+          }
           issued[stage] = true;
           last_phase[stage] = phase;
           if (++stage == kStages) stage = 0, phase ^= 1u;
@@ -170,17 +185,15 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = idesc_mxf4nvf4<kBM, kBN>();
-      const uint32_t sf_a = tmem + Cfg::kSfCol;
-      const uint32_t sf_b = sf_a + 16;
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
+      uint32_t sf_buf = 0;
       bool ok = true, any = false;
       for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
         const GTile tc = grouped_tile(p, t);
         const int k_blocks = p.g[tc.g].k / kBK;
-        const uint32_t sfb_sub = (kBN == 64) ? (uint32_t)((tc.nb & 1) * 2) : 0u;
         if (!ctl.wait(smem_u32(&bar_acc_empty[acc]), acc_phase ^ 1u, kDevTimeoutAccFree)) {
           ok = false;
           break;
@@ -196,23 +209,29 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
           const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
           const uint32_t sb = sa + Cfg::kABytes;
           const uint32_t ssf = sb + Cfg::kBBytes;
+          const uint32_t sf_a = tmem + Cfg::kSfCol + sf_buf * Cfg::kSfBufCols;
+          const uint32_t sf_b = sf_a + 16;
           #pragma unroll
           for (int j = 0; j < kBK / kKStep; ++j) {
             tc_cp_sf_atom(sf_a + 4 * j, sf_atom_desc(ssf + j * kSfAtom));
-            tc_cp_sf_atom(sf_b + 4 * j, sf_atom_desc(ssf + kSfStageBytes + j * kSfAtom));
+            #pragma unroll
+            for (int a = 0; a < Cfg::kSfbAtoms; ++a)
+              tc_cp_sf_atom(sf_b + 4 * (Cfg::kSfbAtoms * j + a),
+                            sf_atom_desc(ssf + (1 + a) * kSfStageBytes + j * kSfAtom));
           }
           #pragma unroll
           for (int j = 0; j < kBK / kKStep; ++j) {
             tc_mma_nvf4(d, kmajor_sw128_desc(sa + 32 * j), kmajor_sw128_desc(sb + 32 * j), idesc,
-                        sf_a + 4 * j, sf_b + 4 * j + sfb_sub, (kb | j) != 0);
+                        sf_a + 4 * j, sf_b + 4 * Cfg::kSfbAtoms * j, (kb | j) != 0);
           }
           tc_commit(smem_u32(&bar_empty[stage]));
           any = true;
+          sf_buf ^= 1u;
           if (++stage == kStages) stage = 0, phase ^= 1u;
         }
         if (!ok) break;
         tc_commit(smem_u32(&bar_acc_full[acc]));
-        if (++acc == Cfg::kAccBufs) acc = 0, acc_phase ^= 1u;
+        if (++acc == kAccBufs) acc = 0, acc_phase ^= 1u;
       }
       if (!ok && any) {
         tc_commit(smem_u32(&bar_drain));
@@ -221,7 +240,10 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int quad = warp & 3;
+    const int quad = warp & 3;        // TMEM lane quadrant this warp may access
+    const int part = warp >> 2;       // which column slice of the tile
+    constexpr int kCW = Cfg::kColsPerWarp;
+    constexpr int kChunks = kCW / 32;
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
@@ -229,17 +251,12 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
       const GroupInfo& gi = p.g[tc.g];
       if (!ctl.wait(smem_u32(&bar_acc_full[acc]), acc_phase, kDevTimeoutAccFull)) break;
       tc_fence_after();
-      const uint32_t t_acc = tmem + ((uint32_t)(quad * 32) << 16) + acc * kBN;
+      const uint32_t t_acc = tmem + ((uint32_t)(quad * 32) << 16) + acc * kBN + part * kCW;
       const int row = tc.mb * kBM + quad * 32 + (int)lane;
-      const int col0 = tc.nb * kBN;
+      const int col0 = tc.nb * kBN + part * kCW;
       __half* crow = gi.c + ((size_t)tc.l * gi.m + row) * (size_t)gi.n + col0;
       const bool row_ok = row < gi.m;
-      #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(t_acc + 32 * c, v);
-        tmem_ld_wait();
-        tmem_regs_ready(v);
+      auto store32 = [&](const uint32_t (&v)[32], int c) {
         #pragma unroll
         for (int q = 0; q < 4; ++q) {
           const int col = col0 + 32 * c + 8 * q;
@@ -252,11 +269,34 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
                          pack_half2(__uint_as_float(v[i + 6]), __uint_as_float(v[i + 7])));
           }
         }
+      };
+      if constexpr (kAccBufs == 1) {
+        // pull the whole slice into registers, hand TMEM back, then store
+        uint32_t v[kChunks][32];
+        #pragma unroll
+        for (int c = 0; c < kChunks; ++c) tmem_ld_32x32b_x32(t_acc + 32 * c, v[c]);
+        tmem_ld_wait();
+        #pragma unroll
+        for (int c = 0; c < kChunks; ++c) tmem_regs_ready(v[c]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[acc]));
+        #pragma unroll
+        for (int c = 0; c < kChunks; ++c) store32(v[c], c);
+      } else {
+        #pragma unroll 1
+        for (int c = 0; c < kChunks; ++c) {
+          uint32_t v[32];
+          tmem_ld_32x32b_x32(t_acc + 32 * c, v);
+          tmem_ld_wait();
+          tmem_regs_ready(v);
+          store32(v, c);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[acc]));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[acc]));
-      if (++acc == Cfg::kAccBufs) acc = 0, acc_phase ^= 1u;
+      if (++acc == kAccBufs) acc = 0, acc_phase ^= 1u;
     }
   }
 

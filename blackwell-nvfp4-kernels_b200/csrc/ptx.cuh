@@ -211,35 +211,6 @@ __device__ __forceinline__ void tc_mma_nvf4(uint32_t d_tmem, uint64_t a_desc, ui
       : "memory");
 }
 
-// Same, keeping the A operand in the tensor core's collector buffer for the
-// next MMA (fill) or taking it from there and releasing it (lastuse).
-__device__ __forceinline__ void tc_mma_nvf4_a_fill(uint32_t d_tmem, uint64_t a_desc,
-                                                   uint64_t b_desc, uint32_t idesc,
-                                                   uint32_t sfa_tmem, uint32_t sfb_tmem,
-                                                   uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %6, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16.collector::a::fill"
-      " [%0], %1, %2, %3, [%4], [%5], p;\n\t"
-      "}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
-      : "memory");
-}
-__device__ __forceinline__ void tc_mma_nvf4_a_lastuse(uint32_t d_tmem, uint64_t a_desc,
-                                                      uint64_t b_desc, uint32_t idesc,
-                                                      uint32_t sfa_tmem, uint32_t sfb_tmem,
-                                                      uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %6, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16.collector::a::lastuse"
-      " [%0], %1, %2, %3, [%4], [%5], p;\n\t"
-      "}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
-      : "memory");
-}
-
 // Arrive (once) on an mbarrier when all previously issued tcgen05 async ops
 // of this thread have completed.
 __device__ __forceinline__ void tc_commit(uint32_t bar) {

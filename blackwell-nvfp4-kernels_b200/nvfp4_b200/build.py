@@ -23,7 +23,6 @@ NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
     "-O3", "-lineinfo", "-std=c++17",
     "-Xcompiler", "-fPIC", "-shared", "-cudart", "static",
-    "-DNVFP4_DUAL_A_COLLECTOR=1",
 ]
 
 

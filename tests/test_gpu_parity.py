@@ -135,8 +135,10 @@ def test_dual_full_size_configs_sampled_rows(cfg):
     assert not torch.isnan(out).any()
 
 
+@pytest.mark.parametrize("bn", ["128", "256"])
 @pytest.mark.parametrize("case", range(len(GROUP_TASK_TESTS)))
-def test_group_task_shapes(case):
+def test_group_task_shapes(case, bn, monkeypatch):
+    monkeypatch.setenv("NVFP4_GROUPED_BN", bn)
     m, n, k = GROUP_TASK_TESTS[case]
     data = I.generate_group_input(m, n, k, len(m), seed=1111, device="cuda")
     outs = G.custom_kernel(data)

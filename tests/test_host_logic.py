@@ -1,0 +1,105 @@
+"""CPU: host-side logic that needs no GPU: the grouped plan cache, the
+multi-GPU partitioners, and the multi-rank timing reduction over gloo."""
+import os
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from nvfp4_b200 import inputs as I
+from nvfp4_b200.group_gemm import _Plan
+from nvfp4_b200.shard import imbalance, lpt_assign, n_shard
+
+
+def _groups(ms, k=256, n=128, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    return I.group_from_fp32([(torch.randn(m, k, generator=g), torch.randn(n, k, generator=g))
+                              for m in ms], device="cpu")
+
+
+def test_plan_matches_same_objects_only():
+    abc, _, perm, sizes = _groups([64, 0, 130])
+    plan = _Plan(abc, perm, sizes, table=None, device=None)
+    assert plan.matches(abc, perm, sizes)
+    assert plan.matches(list(abc), list(perm), list(sizes))           # new lists, same tensors
+    swapped = list(abc)
+    swapped[2] = (abc[2][0].clone(), abc[2][1], abc[2][2])
+    assert not plan.matches(swapped, perm, sizes)                      # a replaced tensor
+    assert not plan.matches(abc[:2], perm[:2], sizes[:2])              # a different count
+    sizes2 = list(sizes)
+    sizes2[0] = (64, 128, 256, 2)
+    assert not plan.matches(abc, perm, sizes2)                         # a different size tuple
+
+
+def test_plan_detects_storage_swap():
+    abc, _, perm, sizes = _groups([64, 32])
+    plan = _Plan(abc, perm, sizes, table=None, device=None)
+    a = abc[0][0]
+    a.set_(a.clone())                                                  # same object, new storage
+    assert not plan.matches(abc, perm, sizes)
+
+
+def test_plan_holds_no_strong_references():
+    import gc
+    import weakref
+    abc, _, perm, sizes = _groups([64])
+    plan = _Plan(abc, perm, sizes, table=None, device=None)
+    probe = weakref.ref(abc[0][0])
+    del abc, perm, sizes
+    gc.collect()
+    assert probe() is None
+    assert plan.refs[0][0]() is None
+
+
+@pytest.mark.parametrize("n,world", [(14336, 1), (14336, 2), (14336, 8), (7168, 8), (1000, 3)])
+def test_n_shard_covers_and_aligns(n, world):
+    spans = [n_shard(n, world, r) for r in range(world)]
+    assert spans[0][0] == 0 and spans[-1][1] == n
+    for (a, b), (c, _) in zip(spans, spans[1:]):
+        assert b == c
+    for a, b in spans:
+        assert a % 128 == 0
+        assert b - a >= 0
+    with pytest.raises(ValueError):
+        n_shard(n, world, world)
+
+
+def test_lpt_assignment_config4():
+    ms = I.config4_m_sizes()
+    costs = [float(m) for m in ms]
+    for world in (1, 2, 4, 8):
+        bins = lpt_assign(costs, world)
+        assert sorted(i for b in bins for i in b) == list(range(len(ms)))
+        # LPT guarantee: makespan <= 4/3 OPT; OPT >= max(mean, max item)
+        opt_lb = max(sum(costs) / world, max(costs))
+        assert max(sum(costs[i] for i in b) for b in bins) <= 4 / 3 * opt_lb + 1e-9
+    assert imbalance(costs, lpt_assign(costs, 1)) == 1.0
+
+
+def _rank_main(rank, world, port, out):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    # each rank's device time and FLOP, reduced the way bench.py reduces them
+    t = torch.tensor([1.0 + rank], dtype=torch.float64)
+    f = torch.tensor([10.0 * (rank + 1)], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    dist.all_reduce(f, op=dist.ReduceOp.SUM)
+    if rank == 0:
+        out.put((t.item(), f.item()))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_multi_rank_reduction_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 29500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    assert all(p.exitcode == 0 for p in procs)
+    t, f = q.get(timeout=5)
+    assert t == 2.0 and f == 30.0          # max time over ranks, summed work
