@@ -15,6 +15,7 @@
 
 #include "../../include/nvfp4_b200.h"
 #include "dual_gemm.cuh"
+#include "dual_gemm_pair.cuh"
 #include "grouped_gemm.cuh"
 
 namespace nvfp4 {
@@ -131,6 +132,24 @@ int encode_operand_uncached(CUtensorMap* map, const void* base, int rows, int k,
   return NVFP4_OK;
 }
 
+// Permuted scale tensor viewed as u64 [blocks][K/64][64] (one 512-byte atom =
+// 64 u64), box {64, 4, 1} = the four atoms of one 256-deep K step.  `blocks`
+// counts 128-row blocks over all batches (L * ceil(rows/128)).
+int encode_scales_uncached(CUtensorMap* map, const void* base, int blocks, int k) {
+  const cuuint64_t dims[3] = {64u, (cuuint64_t)(k / 64), (cuuint64_t)blocks};
+  const cuuint64_t strides[2] = {512u, (cuuint64_t)(k / 64) * 512u};
+  const cuuint32_t box[3] = {64u, 4u, 1u};
+  const cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(NVFP4_ERR_CUDA, "cuTensorMapEncodeTiled (scales) failed (%d) blocks=%d k=%d",
+                (int)r, blocks, k);
+  return NVFP4_OK;
+}
+
 // Encoded descriptors are pure functions of (address, rows, K, L, box rows);
 // repeated calls on the same tensors (the common case: weights, persistent
 // activation buffers) reuse them instead of re-encoding.
@@ -153,8 +172,8 @@ std::mutex g_map_mu;
 std::unordered_map<MapKey, CUtensorMap, MapKeyHash> g_maps;
 constexpr size_t kMaxCachedMaps = 8192;
 
-int encode_operand(CUtensorMap* map, const void* base, int rows, int k, int l, int box_rows) {
-  const MapKey key{reinterpret_cast<uintptr_t>(base), rows, k, l, box_rows};
+template <typename Encode>
+int cached_map(CUtensorMap* map, const MapKey& key, Encode encode) {
   {
     std::lock_guard<std::mutex> lk(g_map_mu);
     auto it = g_maps.find(key);
@@ -163,12 +182,24 @@ int encode_operand(CUtensorMap* map, const void* base, int rows, int k, int l, i
       return NVFP4_OK;
     }
   }
-  int rc = encode_operand_uncached(map, base, rows, k, l, box_rows);
+  int rc = encode();
   if (rc) return rc;
   std::lock_guard<std::mutex> lk(g_map_mu);
   if (g_maps.size() >= kMaxCachedMaps) g_maps.clear();
   g_maps.emplace(key, *map);
   return NVFP4_OK;
+}
+
+int encode_scales(CUtensorMap* map, const void* base, int blocks, int k) {
+  // box == -1 marks the scale-tensor view in the shared cache
+  const MapKey key{reinterpret_cast<uintptr_t>(base), blocks, k, 1, -1};
+  return cached_map(map, key, [&] { return encode_scales_uncached(map, base, blocks, k); });
+}
+
+int encode_operand(CUtensorMap* map, const void* base, int rows, int k, int l, int box_rows) {
+  const MapKey key{reinterpret_cast<uintptr_t>(base), rows, k, l, box_rows};
+  return cached_map(map, key,
+                    [&] { return encode_operand_uncached(map, base, rows, k, l, box_rows); });
 }
 
 int check_launch(const char* what) {
@@ -199,6 +230,39 @@ int launch_dual(DeviceState* d, int slot, DualParams& p, cudaStream_t stream) {
   const int grid = p.tiles < d->num_sms ? p.tiles : d->num_sms;
   kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
   return check_launch("dual_gemm_kernel");
+}
+
+template <int kStages>
+int launch_dual_pair(DeviceState* d, int slot, const void* a, const void* b1, const void* b2,
+                     const void* sfa, const void* sfb1, const void* sfb2, void* c, int m, int n,
+                     int k, int l, cudaStream_t stream) {
+  using Cfg = DualPairCfg<kStages>;
+  auto kern = dual_gemm_pair_kernel<kStages>;
+  int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
+  if (rc) return rc;
+  DualPairParams p;
+  memset(&p, 0, sizeof(p));
+  p.c = static_cast<__half*>(c);
+  p.m = m, p.n = n, p.k = k, p.l = l;
+  p.mp_blocks = (m + 2 * kBM - 1) / (2 * kBM);
+  p.n_blocks = (n + Cfg::kBN - 1) / Cfg::kBN;
+  p.k_blocks = k / kBK;
+  p.tiles = l * p.mp_blocks * p.n_blocks;
+  p.sfa_blocks = (m + 127) / 128;
+  p.sfb_blocks = (n + 127) / 128;
+  p.group_m = env_int("NVFP4_DUAL_GROUP_M", 16);
+  if (p.group_m < 1) p.group_m = 1;
+  p.status = d->status;
+  p.wait_limit = wait_limit_cycles();
+  if ((rc = encode_operand(&p.tmap_a, a, m, k, l, kBM))) return rc;
+  if ((rc = encode_operand(&p.tmap_b1, b1, n, k, l, Cfg::kBN))) return rc;
+  if ((rc = encode_operand(&p.tmap_b2, b2, n, k, l, Cfg::kBN))) return rc;
+  if ((rc = encode_scales(&p.tmap_sfa, sfa, l * p.sfa_blocks, k))) return rc;
+  if ((rc = encode_scales(&p.tmap_sfb1, sfb1, l * p.sfb_blocks, k))) return rc;
+  if ((rc = encode_scales(&p.tmap_sfb2, sfb2, l * p.sfb_blocks, k))) return rc;
+  const int pairs = p.tiles < d->num_sms / 2 ? p.tiles : d->num_sms / 2;
+  kern<<<2 * pairs, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  return check_launch("dual_gemm_pair_kernel");
 }
 
 // ---------------------------------------------------------------- grouped GEMM
@@ -284,8 +348,14 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
 
-  // Tile choice: 128-wide tiles keep the tensor core fed from shared memory;
-  // when they would leave SMs idle, 64-wide tiles double the tile count.
+  // Kernel choice: single-CTA 128-wide tiles, or 64-wide tiles when those
+  // would leave SMs idle.  The CTA-pair kernel (NVFP4_DUAL_KERNEL=pair) loads
+  // 30% fewer operand bytes per SM but measures slower on B200: its
+  // tcgen05.cp.cta_group::2 scale copies run ~2x longer than the single-CTA
+  // copies and serialise with the MMAs in the tensor pipe.
+  const char* kern_env = getenv("NVFP4_DUAL_KERNEL");
+  if (kern_env && strcmp(kern_env, "pair") == 0)
+    return launch_dual_pair<5>(d, 2, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l, stream);
   const int tiles128 = l * p.m_blocks * ((n + 127) / 128);
   int bn = tiles128 >= 2 * d->num_sms ? 128 : 64;
   const int forced = env_int("NVFP4_DUAL_BN", 0);

@@ -251,42 +251,43 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
   } else {
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;             // TMEM lane quadrant this warp may access
-    const int part = warp >> 2;            // which column slice of the tile
+    const int part = warp >> 2;            // which 64-column slice of the tile
     constexpr int kCW = Cfg::kColsPerWarp;
-    constexpr int kChunks = kCW / 32;
+    static_assert(kCW == 64, "64 columns (one 128-byte fp16 line) per lane");
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
       const TileCoord tc = dual_tile_coord(p, t);
       if (!ctl.wait(smem_u32(&bar_acc_full[acc]), acc_phase, kDevTimeoutAccFull)) break;
       tc_fence_after();
-      const uint32_t t_row = tmem + ((uint32_t)(quad * 32) << 16);
-      const uint32_t t_gate = t_row + acc * Cfg::kAccCols + part * kCW;
+      const uint32_t t_gate = tmem + ((uint32_t)(quad * 32) << 16) + acc * Cfg::kAccCols + part * kCW;
       const uint32_t t_up = t_gate + kBN;
+      // pull gate and up for this lane's row into registers, hand TMEM back
+      uint32_t g[2][32], u[2][32];
+      #pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        tmem_ld_32x32b_x32(t_gate + 32 * c, g[c]);
+        tmem_ld_32x32b_x32(t_up + 32 * c, u[c]);
+      }
+      tmem_ld_wait();
+      #pragma unroll
+      for (int c = 0; c < 2; ++c) tmem_regs_ready(g[c]), tmem_regs_ready(u[c]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[acc]));
+      // each lane writes its own row's 128-byte line (8 x 16 B); measured
+      // faster here than a shuffle-transposed full-line store (the extra
+      // epilogue instructions slow the MMA and TMA warps more than the
+      // partial-line writes cost)
       const int row = tc.mb * kBM + quad * 32 + (int)lane;
       const int col0 = tc.nb * kBN + part * kCW;
-      __half* crow = p.c + ((size_t)tc.l * p.m + row) * (size_t)p.n + col0;
-      const bool row_ok = row < p.m;
-      if constexpr (kAccBufs == 1) {
-        // Load everything, hand TMEM back, then do the math from registers.
-        uint32_t g[kChunks][32], u[kChunks][32];
+      if (row < p.m) {
+        __half* crow = p.c + ((size_t)tc.l * p.m + row) * (size_t)p.n + col0;
         #pragma unroll
-        for (int c = 0; c < kChunks; ++c) {
-          tmem_ld_32x32b_x32(t_gate + 32 * c, g[c]);
-          tmem_ld_32x32b_x32(t_up + 32 * c, u[c]);
-        }
-        tmem_ld_wait();
-        #pragma unroll
-        for (int c = 0; c < kChunks; ++c) tmem_regs_ready(g[c]), tmem_regs_ready(u[c]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[acc]));
-        #pragma unroll
-        for (int c = 0; c < kChunks; ++c) {
+        for (int c = 0; c < 2; ++c) {
           #pragma unroll
           for (int v = 0; v < 4; ++v) {
-            const int col = col0 + 32 * c + 8 * v;
-            if (row_ok && col < p.n) {
+            if (col0 + 32 * c + 8 * v < p.n) {
               uint32_t w[4];
               #pragma unroll
               for (int e = 0; e < 4; ++e) {
@@ -298,33 +299,6 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
             }
           }
         }
-      } else {
-        #pragma unroll 1
-        for (int c = 0; c < kChunks; ++c) {
-          uint32_t g[32], u[32];
-          tmem_ld_32x32b_x32(t_gate + 32 * c, g);
-          tmem_ld_32x32b_x32(t_up + 32 * c, u);
-          tmem_ld_wait();
-          tmem_regs_ready(g);
-          tmem_regs_ready(u);
-          #pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            const int col = col0 + 32 * c + 8 * v;
-            if (row_ok && col < p.n) {
-              uint32_t w[4];
-              #pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int i = 8 * v + 2 * e;
-                w[e] = pack_half2(silu_gate(__uint_as_float(g[i]), __uint_as_float(u[i])),
-                                  silu_gate(__uint_as_float(g[i + 1]), __uint_as_float(u[i + 1])));
-              }
-              st_global_v4(crow + 32 * c + 8 * v, w[0], w[1], w[2], w[3]);
-            }
-          }
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[acc]));
       }
       if (++acc == kAccBufs) acc = 0, acc_phase ^= 1u;
     }

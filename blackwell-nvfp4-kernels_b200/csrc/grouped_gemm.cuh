@@ -252,23 +252,18 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
       if (!ctl.wait(smem_u32(&bar_acc_full[acc]), acc_phase, kDevTimeoutAccFull)) break;
       tc_fence_after();
       const uint32_t t_acc = tmem + ((uint32_t)(quad * 32) << 16) + acc * kBN + part * kCW;
-      const int row = tc.mb * kBM + quad * 32 + (int)lane;
+      const int row0 = tc.mb * kBM + quad * 32;
       const int col0 = tc.nb * kBN + part * kCW;
-      __half* crow = gi.c + ((size_t)tc.l * gi.m + row) * (size_t)gi.n + col0;
-      const bool row_ok = row < gi.m;
-      auto store32 = [&](const uint32_t (&v)[32], int c) {
+      __half* cl0 = gi.c + ((size_t)tc.l * gi.m + row0) * (size_t)gi.n + col0;
+      // one 64-column (128-byte) line per lane at a time
+      auto store_line = [&](const uint32_t (&lo)[32], const uint32_t (&hi)[32], int line) {
+        uint32_t w[32];
         #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int col = col0 + 32 * c + 8 * q;
-          if (row_ok && col < gi.n) {
-            const int i = 8 * q;
-            st_global_v4(crow + 32 * c + 8 * q,
-                         pack_half2(__uint_as_float(v[i + 0]), __uint_as_float(v[i + 1])),
-                         pack_half2(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3])),
-                         pack_half2(__uint_as_float(v[i + 4]), __uint_as_float(v[i + 5])),
-                         pack_half2(__uint_as_float(v[i + 6]), __uint_as_float(v[i + 7])));
-          }
+        for (int e = 0; e < 16; ++e) {
+          w[e] = pack_half2(__uint_as_float(lo[2 * e]), __uint_as_float(lo[2 * e + 1]));
+          w[16 + e] = pack_half2(__uint_as_float(hi[2 * e]), __uint_as_float(hi[2 * e + 1]));
         }
+        store_lines_coalesced(w, cl0 + 64 * line, gi.n, gi.m - row0, gi.n - col0 - 64 * line);
       };
       if constexpr (kAccBufs == 1) {
         // pull the whole slice into registers, hand TMEM back, then store
@@ -282,15 +277,17 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[acc]));
         #pragma unroll
-        for (int c = 0; c < kChunks; ++c) store32(v[c], c);
+        for (int c = 0; c < kChunks; c += 2) store_line(v[c], v[c + 1], c / 2);
       } else {
         #pragma unroll 1
-        for (int c = 0; c < kChunks; ++c) {
-          uint32_t v[32];
-          tmem_ld_32x32b_x32(t_acc + 32 * c, v);
+        for (int c = 0; c < kChunks; c += 2) {
+          uint32_t lo[32], hi[32];
+          tmem_ld_32x32b_x32(t_acc + 32 * c, lo);
+          tmem_ld_32x32b_x32(t_acc + 32 * c + 32, hi);
           tmem_ld_wait();
-          tmem_regs_ready(v);
-          store32(v, c);
+          tmem_regs_ready(lo);
+          tmem_regs_ready(hi);
+          store_line(lo, hi, c / 2);
         }
         tc_fence_before();
         __syncwarp();

@@ -68,4 +68,41 @@ __device__ __forceinline__ void st_global_v4(void* p, uint32_t a, uint32_t b, ui
                : "memory");
 }
 
+// Coalesced store of one 128-byte line per lane.
+//
+// On entry lane L holds, in w[0..31], the fp16 line of its own output row
+// (row lane0_row + L, columns [col0, col0 + 64)), as sixteen-byte chunks
+// w[4c..4c+3], c = 0..7.  Each group of 8 lanes transposes its 8x8 matrix
+// of chunks with three xor-butterfly exchanges, after which chunk c of lane
+// i holds chunk i of row 8*group + c; store c then writes four complete
+// lines per warp instead of 32 sixteen-byte pieces of 32 different lines.
+// `c_line0` points at (lane 0's row, col0); rows_left / cols_left bound the
+// valid rows after lane 0's row and the valid columns after col0.
+__device__ __forceinline__ void store_lines_coalesced(uint32_t (&w)[32], __half* c_line0,
+                                                      size_t ld, int rows_left, int cols_left) {
+  const int lane = (int)(threadIdx.x & 31u);
+  const int i = lane & 7, grp = lane >> 3;
+  #pragma unroll
+  for (int s = 1; s < 8; s <<= 1) {
+    const bool hi = (i & s) != 0;
+    #pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      if (c & s) continue;           // pair (c, c | s)
+      #pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const uint32_t send = hi ? w[4 * c + e] : w[4 * (c | s) + e];
+        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, s);
+        if (hi) w[4 * c + e] = recv; else w[4 * (c | s) + e] = recv;
+      }
+    }
+  }
+  #pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    const int r = 8 * grp + c;
+    if (r < rows_left && 8 * i < cols_left)
+      st_global_v4(c_line0 + (size_t)r * ld + 8 * i, w[4 * c], w[4 * c + 1], w[4 * c + 2],
+                   w[4 * c + 3]);
+  }
+}
+
 }  // namespace nvfp4

@@ -72,10 +72,23 @@ def run_dual(data):
     return out.cpu().numpy()
 
 
+@pytest.mark.parametrize("kernel", ["auto", "pair"])
 @pytest.mark.parametrize("m,n,k,l", DUAL_TASK_TESTS)
-def test_dual_task_shapes(m, n, k, l):
+def test_dual_task_shapes(m, n, k, l, kernel, monkeypatch):
+    if kernel != "auto":
+        monkeypatch.setenv("NVFP4_DUAL_KERNEL", kernel)
     data = I.generate_dual_input(m, n, k, l, seed=1111, device="cuda")
-    assert_close(run_dual(data), oracle_dual(data), f"dual {m}x{n}x{k}")
+    assert_close(run_dual(data), oracle_dual(data), f"dual {kernel} {m}x{n}x{k}")
+
+
+@pytest.mark.parametrize("m,n,k,l", [(256, 128, 256, 1), (384, 640, 1024, 2), (200, 264, 512, 1),
+                                     (130, 72, 768, 1), (1, 8, 256, 1), (1000, 1000, 2048, 1)])
+def test_dual_pair_kernel_edges(m, n, k, l, monkeypatch):
+    """CTA-pair kernel: M not a multiple of 256 (second CTA partly or wholly
+    past M), N not a multiple of 128, batched L."""
+    monkeypatch.setenv("NVFP4_DUAL_KERNEL", "pair")
+    data = I.generate_dual_input(m, n, k, l, seed=7 + m + n, device="cuda")
+    assert_close(run_dual(data), oracle_dual(data), f"dual pair {m}x{n}x{k}x{l}")
 
 
 @pytest.mark.parametrize("bn", ["64", "128"])
