@@ -50,11 +50,22 @@ int fail(int code, const char* fmt, ...) {
 
 constexpr int kMaxDevices = 64;
 
+// Split-K scratch of one stream: fp32 partial slots and per-tile counters.
+// Kernels on one stream run in order, so a stream never races with itself;
+// different streams get different scratch.
+struct Workspace {
+  float* partials = nullptr;
+  size_t partial_bytes = 0;
+  int* counters = nullptr;
+  size_t counter_count = 0;
+};
+
 struct DeviceState {
   bool ready = false;
   int num_sms = 0;
   unsigned* status = nullptr;
-  bool smem_set[16] = {};  // one slot per kernel instantiation
+  bool smem_set[32] = {};  // one slot per kernel instantiation
+  std::unordered_map<cudaStream_t, Workspace> ws;
 };
 
 std::mutex g_mu;
@@ -218,17 +229,86 @@ int set_smem_once(DeviceState* d, int slot, Kern kern, int bytes) {
   return NVFP4_OK;
 }
 
+// Grow (never shrink) the stream's split-K scratch; counters start at zero
+// and every kernel leaves them at zero.
+int get_workspace(DeviceState* d, cudaStream_t stream, size_t partial_bytes, size_t counters,
+                  Workspace** out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  Workspace& w = d->ws[stream];
+  if (w.partial_bytes < partial_bytes) {
+    if (w.partials) cudaFree(w.partials);
+    w.partials = nullptr;
+    w.partial_bytes = 0;
+    cudaError_t e = cudaMalloc(&w.partials, partial_bytes);
+    if (e != cudaSuccess)
+      return fail(NVFP4_ERR_CUDA, "split-K workspace (%zu bytes): %s", partial_bytes,
+                  cudaGetErrorString(e));
+    w.partial_bytes = partial_bytes;
+  }
+  if (w.counter_count < counters) {
+    if (w.counters) cudaFree(w.counters);
+    w.counters = nullptr;
+    w.counter_count = 0;
+    cudaError_t e = cudaMalloc(&w.counters, counters * sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(w.counters, 0, counters * sizeof(int));
+    if (e != cudaSuccess)
+      return fail(NVFP4_ERR_CUDA, "split-K counters: %s", cudaGetErrorString(e));
+    w.counter_count = counters;
+  }
+  *out = &w;
+  return NVFP4_OK;
+}
+
+// After a kernel gave up on a wait its counters may be mid-protocol: zero them.
+void reset_workspaces(DeviceState* d) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  for (auto& kv : d->ws)
+    if (kv.second.counters) cudaMemset(kv.second.counters, 0, kv.second.counter_count * sizeof(int));
+}
+
+// Number of K splits for the 128-wide dual kernel: enough work units to give
+// every SM one, each split at least two 256-deep K blocks, at most 16.
+int choose_splits(int tiles, int k_blocks, int num_sms) {
+  if (tiles >= num_sms) return 1;
+  int s = num_sms / tiles;
+  s = s < k_blocks / 2 ? s : k_blocks / 2;
+  s = s < 16 ? s : 16;
+  return s < 1 ? 1 : s;
+}
+
 // ---------------------------------------------------------------- dual GEMM
 template <int kBN, int kStages, int kEpiWarps, int kAccBufs>
 int launch_dual(DeviceState* d, int slot, DualParams& p, cudaStream_t stream) {
   using Cfg = DualCfg<kBN, kStages, kEpiWarps, kAccBufs>;
-  auto kern = dual_gemm_kernel<kBN, kStages, kEpiWarps, kAccBufs>;
-  int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
-  if (rc) return rc;
+  int rc = NVFP4_OK;
   p.n_blocks = (p.n + kBN - 1) / kBN;
   p.tiles = p.l * p.m_blocks * p.n_blocks;
-  const int grid = p.tiles < d->num_sms ? p.tiles : d->num_sms;
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  p.splits = 1;
+  if (kBN == 128) {
+    p.splits = choose_splits(p.tiles, p.k_blocks, d->num_sms);
+    const int forced = env_int("NVFP4_DUAL_SPLITS", 0);
+    if (forced >= 1) p.splits = forced < p.k_blocks ? forced : p.k_blocks;
+  }
+  if (p.splits > 1) {
+    Workspace* w = nullptr;
+    const size_t slot_bytes = (size_t)2 * kBN * kBM * sizeof(float);
+    rc = get_workspace(d, stream, (size_t)p.tiles * p.splits * slot_bytes,
+                       (size_t)p.tiles, &w);
+    if (rc) return rc;
+    p.ws = w->partials;
+    p.ws_ctr = w->counters;
+  }
+  const int units = p.tiles * p.splits;
+  const int grid = units < d->num_sms ? units : d->num_sms;
+  if (p.splits > 1) {
+    auto kern = dual_gemm_kernel<kBN, kStages, kEpiWarps, kAccBufs, true>;
+    if ((rc = set_smem_once(d, slot + 10, kern, Cfg::kSmemBytes))) return rc;
+    kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  } else {
+    auto kern = dual_gemm_kernel<kBN, kStages, kEpiWarps, kAccBufs, false>;
+    if ((rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes))) return rc;
+    kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  }
   return check_launch("dual_gemm_kernel");
 }
 
@@ -356,8 +436,9 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   const char* kern_env = getenv("NVFP4_DUAL_KERNEL");
   if (kern_env && strcmp(kern_env, "pair") == 0)
     return launch_dual_pair<5>(d, 2, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l, stream);
-  const int tiles128 = l * p.m_blocks * ((n + 127) / 128);
-  int bn = tiles128 >= 2 * d->num_sms ? 128 : 64;
+  // 128-wide tiles (one fused N=256 MMA per K step), split along K when
+  // there are fewer tiles than SMs; 64-wide tiles only on request.
+  int bn = 128;
   const int forced = env_int("NVFP4_DUAL_BN", 0);
   if (forced == 64 || forced == 128) bn = forced;
   if ((rc = encode_operand(&p.tmap_a, a, m, k, l, kBM))) return rc;
@@ -420,6 +501,7 @@ extern "C" int nvfp4_device_status(void* stream_, unsigned* bits_out) {
   if (bits) {
     const unsigned zero = 0;
     cudaMemcpy(d->status, &zero, sizeof(zero), cudaMemcpyHostToDevice);
+    reset_workspaces(d);
   }
   if (bits_out) *bits_out = bits;
   if (bits) return fail(NVFP4_ERR_TIMEOUT, "device status bits 0x%x (a bounded wait ran out)", bits);

@@ -23,7 +23,11 @@
 //   MMAs still reading the current ones;
 // * kAccBufs accumulator sets (gate + up, kBN columns each) in TMEM; with one
 //   set the epilogue loads all of its columns to registers and releases TMEM
-//   before doing the math and stores, so the next tile's MMAs start early.
+//   before doing the math and stores, so the next tile's MMAs start early;
+// * split-K for shapes with too few tiles to fill the GPU: each split's
+//   partial gate/up sums go to an fp32 workspace slot; the split that draws
+//   the last ticket sums the slots in split order and alone applies the SiLU
+//   gate (the epilogue is not linear, so the reduction must finish first).
 #pragma once
 #include <cuda.h>
 #include "kernel_common.cuh"
@@ -41,6 +45,11 @@ struct DualParams {
   int m, n, k, l;
   int m_blocks, n_blocks, k_blocks, tiles;
   int group_m;           // raster: M-blocks per group
+  // split-K (splits > 1, 128-wide tiles only): work unit u = tile * splits +
+  // split covers k-blocks [split*k_blocks/splits, (split+1)*k_blocks/splits)
+  int splits;
+  float* ws;             // `splits` fp32 partial slots per tile, [256 cols][128 rows] each
+  int* ws_ctr;           // one ticket counter per tile; zero between calls
   unsigned* status;
   long long wait_limit;
 };
@@ -85,7 +94,20 @@ __device__ __forceinline__ TileCoord dual_tile_coord(const DualParams& p, int t)
   return tc;
 }
 
-template <int kBN, int kStages, int kEpiWarps, int kAccBufs>
+struct KRange { int tile, split, kb0, kb1; };
+
+template <bool kSplitK>
+__device__ __forceinline__ KRange dual_unit(const DualParams& p, int u) {
+  if constexpr (!kSplitK) return KRange{u, 0, 0, p.k_blocks};   // one unit per tile
+  KRange r;
+  r.tile = u / p.splits;
+  r.split = u - r.tile * p.splits;
+  r.kb0 = r.split * p.k_blocks / p.splits;          // splits <= 16: no 32-bit overflow
+  r.kb1 = (r.split + 1) * p.k_blocks / p.splits;
+  return r;
+}
+
+template <int kBN, int kStages, int kEpiWarps, int kAccBufs, bool kSplitK>
 __global__ void __launch_bounds__(DualCfg<kBN, kStages, kEpiWarps, kAccBufs>::kThreads, 1)
 dual_gemm_kernel(const __grid_constant__ DualParams p) {
   using Cfg = DualCfg<kBN, kStages, kEpiWarps, kAccBufs>;
@@ -95,6 +117,7 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
   __shared__ uint64_t bar_drain;
   __shared__ uint32_t s_tmem_base;
   __shared__ volatile int s_abort;
+  __shared__ volatile int s_ticket, s_fail;   // split-K epilogue decisions (uniform after a barrier)
 
   // 1024-byte aligned stage ring (SWIZZLE_128B atoms are 1024 bytes).
   const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
@@ -112,6 +135,7 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
     }
     mbar_init(smem_u32(&bar_drain), 1);
     s_abort = 0;
+    s_fail = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -142,13 +166,15 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
       bool issued[kStages];
       for (int s = 0; s < kStages; ++s) issued[s] = false, last_phase[s] = 0;
       bool ok = true;
-      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
-        const TileCoord tc = dual_tile_coord(p, t);
+      const int units = kSplitK ? p.tiles * p.splits : p.tiles;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const KRange kr = dual_unit<kSplitK>(p, u);
+        const TileCoord tc = dual_tile_coord(p, kr.tile);
         const int n0 = tc.nb * kBN;
         const uint8_t* sfa_t = p.sfa + tc.l * sfa_l + (size_t)tc.mb * rest_k * kSfAtom;
         const uint8_t* sfb1_t = p.sfb1 + tc.l * sfb_l + (size_t)(n0 / 128) * rest_k * kSfAtom;
         const uint8_t* sfb2_t = p.sfb2 + tc.l * sfb_l + (size_t)(n0 / 128) * rest_k * kSfAtom;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kr.kb0; kb < kr.kb1; ++kb) {
           if (!ctl.wait(smem_u32(&bar_empty[stage]), phase ^ 1u, kDevTimeoutStageFree)) {
             ok = false;
             break;
@@ -188,8 +214,10 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
       uint32_t acc_phase = 0;
       uint32_t sf_buf = 0;
       bool ok = true, any = false;
-      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
-        const TileCoord tc = dual_tile_coord(p, t);
+      const int units = kSplitK ? p.tiles * p.splits : p.tiles;
+      for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+        const KRange kr = dual_unit<kSplitK>(p, u);
+        const TileCoord tc = dual_tile_coord(p, kr.tile);
         // 64-wide tiles use half of each 128-row scale atom: columns {0,1} or {2,3}
         const uint32_t sub = (kBN == 64) ? (uint32_t)((tc.nb & 1) * 2) : 0u;
         if (!ctl.wait(smem_u32(&bar_acc_empty[acc]), acc_phase ^ 1u, kDevTimeoutAccFree)) {
@@ -198,7 +226,7 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
         }
         tc_fence_after();
         const uint32_t d_acc = tmem + acc * Cfg::kAccCols;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = kr.kb0; kb < kr.kb1; ++kb) {
           if (!ctl.wait(smem_u32(&bar_full[stage]), phase, kDevTimeoutTmaFull)) {
             ok = false;
             break;
@@ -220,7 +248,7 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
           #pragma unroll
           for (int j = 0; j < kBK / kKStep; ++j) {
             const uint64_t da = kmajor_sw128_desc(sa + 32 * j);
-            const uint32_t accum = (kb | j) != 0;
+            const uint32_t accum = kSplitK ? ((kb != kr.kb0) || (j != 0)) : ((kb | j) != 0);
             if constexpr (kBN == 128) {
               // one N=256 MMA over [B1 ; B2]: the 8 scale columns are exactly
               // SFB1 rows 0..127 then SFB2 rows 0..127
@@ -254,11 +282,25 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
     const int part = warp >> 2;            // which 64-column slice of the tile
     constexpr int kCW = Cfg::kColsPerWarp;
     static_assert(kCW == 64, "64 columns (one 128-byte fp16 line) per lane");
+    constexpr int kEpiThreads = 32 * kEpiWarps;
+    const int et = threadIdx.x;                          // epilogue thread index
+    const int trow = quad * 32 + (int)lane;              // row within the tile
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
-      const TileCoord tc = dual_tile_coord(p, t);
-      if (!ctl.wait(smem_u32(&bar_acc_full[acc]), acc_phase, kDevTimeoutAccFull)) break;
+    const int units = kSplitK ? p.tiles * p.splits : p.tiles;
+    for (int uu = blockIdx.x; uu < units; uu += gridDim.x) {
+      const KRange kr = dual_unit<kSplitK>(p, uu);
+      const TileCoord tc = dual_tile_coord(p, kr.tile);
+      const bool got = ctl.wait(smem_u32(&bar_acc_full[acc]), acc_phase, kDevTimeoutAccFull);
+      if constexpr (!kSplitK) {
+        if (!got) break;
+      } else {
+        // split-K: every epilogue thread must reach each named barrier, so
+        // failures become a shared decision read after the barrier
+        if (!got) s_fail = 1;
+        named_bar_sync(1, kEpiThreads);
+        if (s_fail) break;
+      }
       tc_fence_after();
       const uint32_t t_gate = tmem + ((uint32_t)(quad * 32) << 16) + acc * Cfg::kAccCols + part * kCW;
       const uint32_t t_up = t_gate + kBN;
@@ -275,6 +317,49 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[acc]));
+      if (++acc == kAccBufs) acc = 0, acc_phase ^= 1u;
+      if constexpr (kSplitK) {
+        // Every split publishes its partial in its own slot ([col][row]: a
+        // warp writes 128 contiguous bytes per column), fences, and draws a
+        // ticket; whoever draws the last ticket finds all other partials
+        // already visible, sums all slots in split order (deterministic) and
+        // alone applies the SiLU gate.
+        const size_t slot_elems = (size_t)2 * kBN * kBM;
+        float* slots = p.ws + (size_t)kr.tile * p.splits * slot_elems;
+        float* own = slots + (size_t)kr.split * slot_elems;
+        #pragma unroll
+        for (int c = 0; c < 2; ++c)
+          #pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int col = part * kCW + 32 * c + i;
+            __stcg(own + (size_t)col * kBM + trow, __uint_as_float(g[c][i]));
+            __stcg(own + (size_t)(kBN + col) * kBM + trow, __uint_as_float(u[c][i]));
+          }
+        __threadfence();
+        named_bar_sync(1, kEpiThreads);
+        if (et == 0) s_ticket = atomicAdd(&p.ws_ctr[kr.tile], 1);
+        named_bar_sync(1, kEpiThreads);
+        if (s_ticket != p.splits - 1) continue;
+        __threadfence();
+        if (et == 0) p.ws_ctr[kr.tile] = 0;   // zero again for the next call
+        #pragma unroll
+        for (int c = 0; c < 2; ++c)
+          #pragma unroll
+          for (int i = 0; i < 32; ++i) g[c][i] = u[c][i] = 0u;
+        for (int sp = 0; sp < p.splits; ++sp) {
+          const float* slot = slots + (size_t)sp * slot_elems;
+          #pragma unroll
+          for (int c = 0; c < 2; ++c)
+            #pragma unroll
+            for (int i = 0; i < 32; ++i) {
+              const int col = part * kCW + 32 * c + i;
+              g[c][i] = __float_as_uint(__uint_as_float(g[c][i]) +
+                                        __ldcg(slot + (size_t)col * kBM + trow));
+              u[c][i] = __float_as_uint(__uint_as_float(u[c][i]) +
+                                        __ldcg(slot + (size_t)(kBN + col) * kBM + trow));
+            }
+        }
+      }
       // each lane writes its own row's 128-byte line (8 x 16 B); measured
       // faster here than a shuffle-transposed full-line store (the extra
       // epilogue instructions slow the MMA and TMA warps more than the
@@ -300,7 +385,6 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
           }
         }
       }
-      if (++acc == kAccBufs) acc = 0, acc_phase ^= 1u;
     }
   }
 

@@ -99,6 +99,24 @@ def test_dual_both_tile_widths(m, n, k, l, bn, monkeypatch):
     assert_close(run_dual(data), oracle_dual(data), f"dual bn={bn} {m}x{n}x{k}x{l}")
 
 
+@pytest.mark.parametrize("splits", [2, 3, 5, 16])
+@pytest.mark.parametrize("m,n,k,l", [(256, 512, 4096, 1), (200, 264, 2048, 1), (384, 640, 1024, 2),
+                                     (128, 7168, 4096, 1)])
+def test_dual_split_k(m, n, k, l, splits, monkeypatch):
+    """Split-K reduction (partials in workspace, last split applies SiLU) at
+    forced split counts, ragged M/N and batched L."""
+    monkeypatch.setenv("NVFP4_DUAL_SPLITS", str(splits))
+    data = I.generate_dual_input(m, n, k, l, seed=splits * 31 + m, device="cuda")
+    assert_close(run_dual(data), oracle_dual(data), f"dual splitK={splits} {m}x{n}x{k}x{l}")
+
+
+def test_dual_split_k_deterministic(monkeypatch):
+    monkeypatch.setenv("NVFP4_DUAL_SPLITS", "4")
+    data = I.generate_dual_input(256, 1024, 4096, 1, seed=5, device="cuda")
+    outs = [D.custom_kernel(data).clone() for _ in range(3)]
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+
+
 def test_dual_config0_normal_inputs():
     data = I.dual_config_input(0, device="cuda")
     assert_close(run_dual(data), oracle_dual(data), "dual config 0")
