@@ -66,6 +66,7 @@ struct DeviceState {
   unsigned* status = nullptr;
   bool smem_set[32] = {};  // one slot per kernel instantiation
   std::unordered_map<cudaStream_t, Workspace> ws;
+  unsigned char* noalloc_scratch = nullptr;   // device address of g_noalloc_scratch
 };
 
 std::mutex g_mu;
@@ -533,3 +534,118 @@ extern "C" const char* nvfp4_status_string(int s) {
 extern "C" const char* nvfp4_last_error(void) { return t_last_error; }
 
 extern "C" int nvfp4_version(void) { return 100; }
+
+// ---------------------------------------------------------------------------
+// Dual GEMM without any allocation.
+//
+// For callers that must not allocate device memory at call time: inference
+// servers that reserve the whole HBM budget up front for weights and KV
+// caches and hand out no further bytes, and hosts whose memory manager owns
+// every device allocation (so a library-side cudaMalloc is forbidden or
+// would fragment its pool).  Instead of the per-stream workspace that
+// nvfp4_dual_gemm grows with cudaMalloc, the split-K partials of this entry
+// point live in the fixed array below, which every GPU that loads the
+// library keeps until the process exits.
+// ---------------------------------------------------------------------------
+namespace nvfp4 {
+namespace {
+constexpr size_t kNoAllocPartialBytes = size_t(20) << 20;   // 20 MiB of fp32 partial slots
+constexpr size_t kNoAllocCounterInts = 4096;                // one ticket counter per tile
+constexpr size_t kNoAllocScratchBytes = kNoAllocPartialBytes + kNoAllocCounterInts * sizeof(int);
+}  // namespace
+}  // namespace nvfp4
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[nvfp4::kNoAllocScratchBytes];
+
+namespace nvfp4 {
+namespace {
+
+// Once per device, with that device current: the device address of the
+// scratch array (host code may not use the symbol itself as a pointer).
+int noalloc_scratch(DeviceState* d, unsigned char** out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!d->noalloc_scratch) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(NVFP4_ERR_CUDA, "no-alloc scratch address: %s", cudaGetErrorString(e));
+    d->noalloc_scratch = static_cast<unsigned char*>(ptr);
+  }
+  *out = d->noalloc_scratch;
+  return NVFP4_OK;
+}
+
+}  // namespace
+}  // namespace nvfp4
+
+extern "C" int nvfp4_dual_gemm_noalloc(const void* a, const void* b1, const void* b2,
+                                       const void* sfa, const void* sfb1, const void* sfb2,
+                                       void* c, int m, int n, int k, int l, void* stream_) {
+  if (!a || !b1 || !b2 || !sfa || !sfb1 || !sfb2 || !c)
+    return fail(NVFP4_ERR_INVALID_ARG, "null pointer argument");
+  if (m < 1 || n < 1 || k < 1 || l < 1)
+    return fail(NVFP4_ERR_INVALID_ARG, "sizes must be positive (m=%d n=%d k=%d l=%d)", m, n, k, l);
+  if (k % kBK != 0) return fail(NVFP4_ERR_SHAPE, "K=%d is not a multiple of 256", k);
+  if (n % 8 != 0) return fail(NVFP4_ERR_SHAPE, "N=%d is not a multiple of 8", n);
+  if ((long long)m * n * l >= (1LL << 40) || (long long)(m > n ? m : n) * k * l >= (1LL << 41))
+    return fail(NVFP4_ERR_SHAPE, "problem too large");
+  if (!aligned16(a) || !aligned16(b1) || !aligned16(b2) || !aligned16(sfa) || !aligned16(sfb1) ||
+      !aligned16(sfb2) || !aligned16(c))
+    return fail(NVFP4_ERR_ALIGNMENT, "all operands must be 16-byte aligned");
+  DeviceState* d = nullptr;
+  int rc = get_device(&d);
+  if (rc) return rc;
+  unsigned char* scratch = nullptr;
+  if ((rc = noalloc_scratch(d, &scratch))) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+
+  constexpr int kBN = 128, kStages = 4, kEpiWarps = 8;
+  using Cfg = DualCfg<kBN, kStages, kEpiWarps, 1>;
+  DualParams p;
+  memset(&p, 0, sizeof(p));
+  p.sfa = static_cast<const uint8_t*>(sfa);
+  p.sfb1 = static_cast<const uint8_t*>(sfb1);
+  p.sfb2 = static_cast<const uint8_t*>(sfb2);
+  p.c = static_cast<__half*>(c);
+  p.m = m, p.n = n, p.k = k, p.l = l;
+  p.m_blocks = (m + kBM - 1) / kBM;
+  p.n_blocks = (n + kBN - 1) / kBN;
+  p.k_blocks = k / kBK;
+  p.tiles = l * p.m_blocks * p.n_blocks;
+  p.group_m = env_int("NVFP4_DUAL_GROUP_M", 16);
+  if (p.group_m < 1) p.group_m = 1;
+  p.splits = choose_splits(p.tiles, p.k_blocks, d->num_sms);
+  const int forced = env_int("NVFP4_DUAL_SPLITS", 0);
+  if (forced >= 1) p.splits = forced < p.k_blocks ? forced : p.k_blocks;
+  p.status = d->status;
+  p.wait_limit = wait_limit_cycles();
+  if (p.splits > 1) {
+    const size_t need = (size_t)p.tiles * p.splits * 2 * kBN * kBM * sizeof(float);
+    if (need > kNoAllocPartialBytes || (size_t)p.tiles > kNoAllocCounterInts)
+      return fail(NVFP4_ERR_SHAPE,
+                  "split-K needs %zu bytes of partials for %d tiles x %d splits; the fixed "
+                  "no-alloc scratch holds %zu bytes and %zu tiles",
+                  need, p.tiles, p.splits, kNoAllocPartialBytes, kNoAllocCounterInts);
+    p.ws = reinterpret_cast<float*>(scratch);
+    p.ws_ctr = reinterpret_cast<int*>(scratch + kNoAllocPartialBytes);
+    // the array keeps the previous call's contents: the tickets must start at zero
+    cudaError_t e = cudaMemsetAsync(p.ws_ctr, 0, (size_t)p.tiles * sizeof(int), stream);
+    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "counter reset: %s", cudaGetErrorString(e));
+  }
+  // descriptors are encoded on the stack every call (the cache would allocate host memory)
+  if ((rc = encode_operand_uncached(&p.tmap_a, a, m, k, l, kBM))) return rc;
+  if ((rc = encode_operand_uncached(&p.tmap_b1, b1, n, k, l, kBN))) return rc;
+  if ((rc = encode_operand_uncached(&p.tmap_b2, b2, n, k, l, kBN))) return rc;
+  const int units = p.tiles * p.splits;
+  const int grid = units < d->num_sms ? units : d->num_sms;
+  if (p.splits > 1) {
+    auto kern = dual_gemm_kernel<kBN, kStages, kEpiWarps, 1, true>;
+    if ((rc = set_smem_once(d, 20, kern, Cfg::kSmemBytes))) return rc;
+    kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  } else {
+    auto kern = dual_gemm_kernel<kBN, kStages, kEpiWarps, 1, false>;
+    if ((rc = set_smem_once(d, 21, kern, Cfg::kSmemBytes))) return rc;
+    kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+  }
+  return check_launch("dual_gemm_kernel (no-alloc)");
+}

@@ -22,6 +22,7 @@ NVFP4_ERR_TIMEOUT = -6
 # every symbol include/nvfp4_b200.h declares
 EXPORTED = (
     "nvfp4_dual_gemm",
+    "nvfp4_dual_gemm_noalloc",
     "nvfp4_grouped_gemm",
     "nvfp4_device_status",
     "nvfp4_wait_selftest",
@@ -69,6 +70,8 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
     vp, i32 = ctypes.c_void_p, ctypes.c_int
     lib.nvfp4_dual_gemm.argtypes = [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]
     lib.nvfp4_dual_gemm.restype = i32
+    lib.nvfp4_dual_gemm_noalloc.argtypes = [vp, vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp]
+    lib.nvfp4_dual_gemm_noalloc.restype = i32
     lib.nvfp4_grouped_gemm.argtypes = [ctypes.POINTER(Group), i32, vp]
     lib.nvfp4_grouped_gemm.restype = i32
     lib.nvfp4_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint)]

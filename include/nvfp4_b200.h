@@ -53,6 +53,21 @@ int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, const void* s
                     const void* sfb1_perm, const void* sfb2_perm, void* c, int m, int n, int k,
                     int l, void* stream);
 
+/* The dual GEMM above, for callers that may not allocate device memory at
+ * call time (servers that hand the whole HBM budget to weights and KV caches
+ * up front; hosts whose own memory manager must own every device byte).  It
+ * allocates nothing: when the shape is split along K, the partial sums live
+ * in a fixed array inside this library (20 MiB of partials + 16 KiB of
+ * counters, held by every GPU that loads the library until exit), and shapes
+ * whose split needs more are rejected with NVFP4_ERR_SHAPE.  The first call on
+ * a device looks up that array's device address; make that first call before
+ * any stream capture.  All calls share the one array: calls that overlap on
+ * the GPU (e.g. on two streams at once) race.  No counterpart in the
+ * reference. */
+int nvfp4_dual_gemm_noalloc(const void* a, const void* b1, const void* b2, const void* sfa_perm,
+                            const void* sfb1_perm, const void* sfb2_perm, void* c, int m, int n,
+                            int k, int l, void* stream);
+
 /* C_g = A_g . B_gᵀ for g in [0, num_groups) in one persistent launch (the host
  * splits tables larger than one launch's parameter block).  Groups with
  * M == 0 are skipped.  Replaces module.kernel_launch(As,Bs,SFAs,SFBs,Cs,
