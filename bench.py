@@ -94,12 +94,31 @@ def group_workload(cfg: int, rank: int, world: int, device):
     return data, flop, nbytes, desc
 
 
+def quant_workload(rank, world, device):
+    """Configuration 5: quantise configuration 1's fp32 operands (A, B1, B2)
+    to NVFP4 on the device; HBM-bound."""
+    from nvfp4_b200 import inputs as I
+    spec = I.DUAL_CONFIGS[1]
+    m, n, k = spec["m"], spec["n"], spec["k"]
+    g = torch.Generator().manual_seed(spec["seed"] * 1000 + rank)
+    xs = [torch.randn(r, k, generator=g).to(device) for r in (m, n, n)]
+    elems = sum(x.numel() for x in xs)
+    nbytes = elems * 4 + elems // 2 + elems // 16 * 2      # fp32 in, e2m1 + two scale layouts out
+    desc = dict(workload="quantize_cfg1_operands", rows=[m, n, n], k=k)
+    return xs, 0.0, nbytes, desc
+
+
 def make_workload(cfg, rank, world, device):
+    if cfg == 5:
+        return quant_workload(rank, world, device)
     return dual_workload(cfg, rank, world, device) if cfg in (0, 1, 2) else \
         group_workload(cfg, rank, world, device)
 
 
 def call(cfg, data):
+    if cfg == 5:
+        from nvfp4_b200.quantize import quantize
+        return [quantize(x) for x in data]
     if cfg in (0, 1, 2):
         from nvfp4_b200.dual_gemm import custom_kernel
     else:
@@ -109,6 +128,8 @@ def call(cfg, data):
 
 def device_tensors(cfg, data):
     """(input tensors a user would ship each step, output tensors)."""
+    if cfg == 5:
+        return list(data), []
     if cfg in (0, 1, 2):
         return [data[0], data[1], data[2], data[6], data[7], data[8]], [data[9]]
     abc, _, perm, sizes = data
@@ -267,6 +288,8 @@ def load_traffic(workload: str):
 
 
 def metric_name(cfg):
+    if cfg == 5:
+        return "NVFP4 quantisation bandwidth (fp32 -> e2m1 + e4m3 scales)"
     return "NVFP4 effective TFLOPS (dual GEMM)" if cfg in (0, 1, 2) else \
         "NVFP4 effective TFLOPS (grouped GEMM)"
 
@@ -276,7 +299,8 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4])
+    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4, 5],
+                    help="0-4: BASELINE configurations; 5: device quantisation of config 1's operands")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
@@ -339,14 +363,22 @@ def main():
         pg.all_reduce(flop_t, op=pg.ReduceOp.SUM)
     t_max_s = t_total.item() / 1e3
     total_flop = flop_t.item() * args.steps
-    value = total_flop / t_max_s / 1e12
     ms_per_step = t_max_s * 1e3 / args.steps
+    if cfg == 5:   # bytes-moved metric for the quantiser
+        bytes_t = torch.tensor([float(nbytes)], dtype=torch.float64, device=device)
+        if pg:
+            pg.all_reduce(bytes_t, op=pg.ReduceOp.SUM)
+        value = bytes_t.item() * args.steps / t_max_s / 1e9
+    else:
+        value = total_flop / t_max_s / 1e12
 
     if args.kernel_only:
         if rank == 0:
             print(json.dumps({"metric": metric_name(cfg), "value": round(value, 2),
-                              "unit": "TFLOP/s", "us_per_call": round(ms_per_step * 1e3, 2),
-                              "config": desc, "kernel_only": True}), flush=True)
+                              "unit": "GB/s" if cfg == 5 else "TFLOP/s",
+                              "us_per_call": round(ms_per_step * 1e3, 2),
+                              "config": desc, "kernel_only": True, "clocks": clk.summary()}),
+                  flush=True)
         if pg:
             pg.destroy_process_group()
         return

@@ -17,6 +17,7 @@
 #include "dual_gemm.cuh"
 #include "dual_gemm_pair.cuh"
 #include "grouped_gemm.cuh"
+#include "quantize.cuh"
 
 namespace nvfp4 {
 
@@ -534,6 +535,34 @@ extern "C" const char* nvfp4_status_string(int s) {
 extern "C" const char* nvfp4_last_error(void) { return t_last_error; }
 
 extern "C" int nvfp4_version(void) { return 100; }
+
+extern "C" int nvfp4_quantize(const float* x, int rows, int k, int l, void* packed,
+                              void* sf_perm, void* sf_plain, void* stream_) {
+  if (!x || !packed || !sf_perm) return fail(NVFP4_ERR_INVALID_ARG, "null pointer argument");
+  if (rows < 1 || k < 1 || l < 1)
+    return fail(NVFP4_ERR_INVALID_ARG, "sizes must be positive (rows=%d k=%d l=%d)", rows, k, l);
+  if (k % 64 != 0) return fail(NVFP4_ERR_SHAPE, "K=%d is not a multiple of 64", k);
+  const int row_blocks = (rows + 127) / 128;
+  if (row_blocks > 65535 || l > 65535 || (long long)rows * k * l >= (1LL << 40))
+    return fail(NVFP4_ERR_SHAPE, "problem too large");
+  if (!aligned16(x) || !aligned16(packed) || !aligned16(sf_perm) ||
+      (sf_plain && (reinterpret_cast<uintptr_t>(sf_plain) & 3u)))
+    return fail(NVFP4_ERR_ALIGNMENT, "x/packed/sf_perm need 16-byte, sf_plain 4-byte alignment");
+  DeviceState* d = nullptr;
+  int rc = get_device(&d);
+  if (rc) return rc;
+  QuantParams p;
+  p.x = x;
+  p.packed = static_cast<uint8_t*>(packed);
+  p.sf_perm = static_cast<uint8_t*>(sf_perm);
+  p.sf_plain = static_cast<uint8_t*>(sf_plain);
+  p.rows = rows, p.k = k, p.l = l;
+  p.row_blocks = row_blocks;
+  p.k_atoms = k / 64;
+  const dim3 grid(p.k_atoms, row_blocks, l);
+  quantize_nvfp4_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream_)>>>(p);
+  return check_launch("quantize_nvfp4_kernel");
+}
 
 // ---------------------------------------------------------------------------
 // Dual GEMM without any allocation.

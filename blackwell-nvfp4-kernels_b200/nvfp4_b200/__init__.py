@@ -7,8 +7,8 @@ it through ctypes.
     from nvfp4_b200.dual_gemm import custom_kernel    # dual GEMM task
     from nvfp4_b200.group_gemm import custom_kernel   # grouped GEMM task
 """
-from . import dual_gemm, formats, group_gemm, inputs  # noqa: F401
+from . import dual_gemm, formats, group_gemm, inputs, quantize  # noqa: F401
 from ._lib import Nvfp4Error, device_status, load  # noqa: F401
 
-__all__ = ["dual_gemm", "group_gemm", "formats", "inputs", "load", "device_status",
+__all__ = ["dual_gemm", "group_gemm", "formats", "inputs", "quantize", "load", "device_status",
            "Nvfp4Error"]

@@ -24,6 +24,7 @@ EXPORTED = (
     "nvfp4_dual_gemm",
     "nvfp4_dual_gemm_noalloc",
     "nvfp4_grouped_gemm",
+    "nvfp4_quantize",
     "nvfp4_device_status",
     "nvfp4_wait_selftest",
     "nvfp4_status_string",
@@ -74,6 +75,8 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
     lib.nvfp4_dual_gemm_noalloc.restype = i32
     lib.nvfp4_grouped_gemm.argtypes = [ctypes.POINTER(Group), i32, vp]
     lib.nvfp4_grouped_gemm.restype = i32
+    lib.nvfp4_quantize.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp]
+    lib.nvfp4_quantize.restype = i32
     lib.nvfp4_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint)]
     lib.nvfp4_device_status.restype = i32
     lib.nvfp4_wait_selftest.argtypes = [ctypes.c_longlong, vp]

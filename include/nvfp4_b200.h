@@ -74,6 +74,17 @@ int nvfp4_dual_gemm_noalloc(const void* a, const void* b1, const void* b2, const
  * problem_sizes) (nvfp4_group_gemm/submission_v7.py:454-522). */
 int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream);
 
+/* Quantise fp32 x [L][rows][K] (K % 64 == 0) to NVFP4 on the device:
+ * packed e2m1 [L][rows][K/2] (element 2i in the low nibble), the permuted
+ * scale atoms [L][ceil(rows/128)][K/64][32][4][4] the GEMMs read (padding rows
+ * get zero scales) and, if sf_plain is not NULL, the plain scales
+ * [L][rows][K/16].  Per 16-element block: scale = e4m3_rne(amax/6), value =
+ * e2m1_rne(x/scale) (ties to even, saturating), zero scale -> zero values.
+ * No kernel counterpart in the reference: it is the host-side input
+ * construction of nvfp4_dual_gemm/reference.py:113-187 moved on-device. */
+int nvfp4_quantize(const float* x, int rows, int k, int l, void* packed, void* sf_perm,
+                   void* sf_plain, void* stream);
+
 /* Synchronises `stream`, then reads and clears this device's status word.
  * Returns NVFP4_ERR_TIMEOUT if a kernel gave up on a wait (bits in *bits_out,
  * may be NULL), NVFP4_ERR_CUDA on a CUDA error, else NVFP4_OK.  No reference

@@ -80,6 +80,15 @@ def test_grouped_rejects_bad_arguments_without_gpu(lib):
     assert lib.nvfp4_grouped_gemm(t, 1, None) == _lib.NVFP4_OK
 
 
+def test_quantize_rejects_bad_arguments_without_gpu(lib):
+    p = ctypes.c_void_p(4096)
+    f = lib.nvfp4_quantize
+    assert f(None, 128, 64, 1, p, p, None, None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert f(p, 128, 96, 1, p, p, None, None) == _lib.NVFP4_ERR_SHAPE
+    assert f(p, 128, 64, 1, ctypes.c_void_p(4096 + 4), p, None, None) == _lib.NVFP4_ERR_ALIGNMENT
+    assert f(p, 128, 64, 1, p, p, ctypes.c_void_p(4097), None) == _lib.NVFP4_ERR_ALIGNMENT
+
+
 def test_check_raises_with_detail(lib):
     p = ctypes.c_void_p(4096)
     st = lib.nvfp4_dual_gemm(p, p, p, p, p, p, p, 128, 128, 320, 1, None)

@@ -1,0 +1,68 @@
+"""GPU: the device quantiser (nvfp4_quantize) is bit-exact against the oracle
+restatement of the quantisation and of the scale layouts, and its output
+feeds the dual GEMM to the oracle's result."""
+import numpy as np
+import pytest
+import torch
+
+from nvfp4_b200 import _lib
+from nvfp4_b200 import build as B
+from nvfp4_b200 import dual_gemm as D
+from nvfp4_b200.quantize import quantize
+from oracle import nvfp4_oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _ready(cuda_device):
+    B.build()
+    _lib.load()
+
+
+def _edge_rows(k):
+    mags = np.array([0, 0.25, 0.5, 0.75, 1, 1.25, 1.5, 1.75, 2, 2.5, 3, 3.5, 4, 5, 6, 7, 1e4, 3e3],
+                    np.float32)
+    row = np.zeros(k, np.float32)
+    vals = np.concatenate([mags, -mags])
+    row[: len(vals)] = vals[:k]
+    return row
+
+
+@pytest.mark.parametrize("rows,k,l,scale", [(128, 64, 1, 1.0), (200, 1024, 1, 3.0),
+                                            (1, 256, 2, 0.01), (385, 4096, 1, 1e3),
+                                            (256, 7168, 1, 1.0)])
+def test_quantize_bit_exact(rows, k, l, scale):
+    g = torch.Generator().manual_seed(rows + k)
+    x = torch.randn(l, rows, k, generator=g) * scale
+    x[0, 0] = torch.from_numpy(_edge_rows(k))     # ties, saturation, large amax
+    if rows > 1:
+        x[0, 1, :16] = 0.0                        # zero block -> zero scale
+        x[0, 1, 16:32] = 1e-12                    # scale underflows to zero
+    packed, sf, sf_perm = quantize(x.cuda())
+    assert _lib.device_status() == 0
+    for b in range(l):
+        po, so = O.quantize_nvfp4(x[b].numpy())
+        assert np.array_equal(packed.view(torch.uint8)[:, :, b].cpu().numpy(), po)
+        assert np.array_equal(sf.view(torch.uint8)[:, :, b].cpu().numpy(), so)
+    mem = sf_perm.view(torch.uint8).permute(5, 2, 4, 0, 1, 3).contiguous().cpu().numpy()
+    assert np.array_equal(mem, O.permuted_sf(sf.view(torch.uint8).cpu().numpy()))
+
+
+def test_quantize_feeds_dual_gemm():
+    m, n, k = 256, 384, 1024
+    g = torch.Generator().manual_seed(11)
+    qa = quantize(torch.randn(m, k, generator=g).cuda())
+    q1 = quantize(torch.randn(n, k, generator=g).cuda())
+    q2 = quantize(torch.randn(n, k, generator=g).cuda())
+    c = torch.zeros((1, m, n), dtype=torch.float16, device="cuda").permute(1, 2, 0)
+    data = (qa[0], q1[0], q2[0], qa[1], q1[1], q2[1], qa[2], q1[2], q2[2], c)
+    out = D.custom_kernel(data).cpu().numpy()
+    u8 = lambda t: t.cpu().view(torch.uint8).numpy()
+    want = O.ref_dual_batched(u8(qa[0]), u8(q1[0]), u8(q2[0]), u8(qa[1]), u8(q1[1]), u8(q2[1]))
+    assert O.allclose_report(out, want, 1e-2, 1e-2)[0] == 0
+
+
+def test_quantize_rejects_bad_k():
+    with pytest.raises(ValueError):
+        quantize(torch.zeros(4, 100, device="cuda"))
