@@ -560,7 +560,7 @@ extern "C" int nvfp4_quantize(const float* x, int rows, int k, int l, void* pack
   p.row_blocks = row_blocks;
   p.k_atoms = k / 64;
   const dim3 grid(p.k_atoms, row_blocks, l);
-  quantize_nvfp4_kernel<<<grid, 128, 0, static_cast<cudaStream_t>(stream_)>>>(p);
+  quantize_nvfp4_kernel<<<grid, kQuantThreads, 0, static_cast<cudaStream_t>(stream_)>>>(p);
   return check_launch("quantize_nvfp4_kernel");
 }
 

@@ -9,13 +9,11 @@
 // and has no quantiser; the quantisation is the one the benchmark
 // configurations define, the same as nvfp4_b200.formats.quantize_nvfp4:
 //   scale = e4m3_rne(amax / 6)   (saturating at 448; CUDA's RNE fp8 conversion)
-//   value = e2m1_rne(x / scale)  (IEEE division; ties to the even code; saturating at 6)
+//   value = e2m1_rne(x / scale)  (IEEE division; ties to the even code; saturating at 6;
+//                                 a value rounding to zero keeps its sign)
 //   scale == 0 -> all values 0.
 //
-// One CTA of 128 threads per (128-row block, 64-deep K atom): thread i owns row
-// i of the block and its four 16-element blocks, writes 32 packed bytes and the
-// 4-byte word of the scale atom at (i % 32) * 16 + (i / 32) * 4, so the CTA
-// writes the whole 512-byte atom.  HBM-bound: 4.5625 bytes per element.
+// HBM-bound: 4 bytes read and 0.5625 (+0.0625 plain scales) written per element.
 #pragma once
 #include <cuda_fp8.h>
 #include <cstdint>
@@ -31,62 +29,87 @@ struct QuantParams {
   int row_blocks, k_atoms;
 };
 
-// e2m1 code (0..15) of q with round-to-nearest-even on the magnitude grid
-// {0, .5, 1, 1.5, 2, 3, 4, 6}; a tie is resolved toward the even code.
-__device__ __forceinline__ uint32_t e2m1_code(float q) {
-  const float a = fabsf(q);
-  uint32_t c = (a > 0.25f) + (a >= 0.75f) + (a > 1.25f) + (a >= 1.75f) + (a > 2.5f) +
-               (a >= 3.5f) + (a > 5.0f);
-  return c | ((c != 0u && signbit(q)) ? 8u : 0u);
+// Two fp32 values -> one byte of e2m1 codes (lo in the low nibble), rounded
+// to nearest even and saturated to +-6 by the sm_100 conversion instruction
+// (a value rounding to zero keeps its sign).
+__device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
+  uint32_t r;
+  asm("{\n\t.reg .b8 t;\n\t"
+      "cvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\t"
+      "cvt.u32.u8 %0, t;\n\t}"
+      : "=r"(r)
+      : "f"(hi), "f"(lo));
+  return r;
 }
 
-__global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const QuantParams p) {
+// One CTA of 256 threads per (128-row block, 64-deep K atom).  Lane j of a
+// warp handles 8 consecutive values of row (4*step + j/8): a warp reads four
+// whole 256-byte row segments per step (coalesced), the two lanes of a
+// 16-element block combine their amax with one shuffle, each lane writes its
+// 4 packed bytes, and the row's four scale bytes are gathered into one
+// 4-byte word of the scale atom (byte (r%32)*16 + ((r/32)%4)*4 + block).
+constexpr int kQuantThreads = 256;
+
+__global__ void __launch_bounds__(kQuantThreads) quantize_nvfp4_kernel(const QuantParams p) {
   const int atom = blockIdx.x;                 // k-atom index (64 K per atom)
   const int rb = blockIdx.y;                   // 128-row block
   const int l = blockIdx.z;
-  const int i = threadIdx.x;
-  const int row = rb * 128 + i;
-  uint32_t sf_word = 0;
-  if (row < p.rows) {
-    const float* src = p.x + ((size_t)l * p.rows + row) * (size_t)p.k + (size_t)atom * 64;
-    uint32_t packed[8];
-    #pragma unroll
-    for (int b = 0; b < 4; ++b) {               // four 16-element scale blocks
-      float v[16];
-      #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float4 f = __ldcs(reinterpret_cast<const float4*>(src + 16 * b + 4 * q));
-        v[4 * q] = f.x, v[4 * q + 1] = f.y, v[4 * q + 2] = f.z, v[4 * q + 3] = f.w;
-      }
-      float amax = 0.f;
-      #pragma unroll
-      for (int e = 0; e < 16; ++e) amax = fmaxf(amax, fabsf(v[e]));
-      const __nv_fp8_storage_t s8 =
-          __nv_cvt_float_to_fp8(__fdiv_rn(amax, 6.0f), __NV_SATFINITE, __NV_E4M3);
-      const float s = __half2float(__half(__nv_cvt_fp8_to_halfraw(s8, __NV_E4M3)));
-      sf_word |= (uint32_t)s8 << (8 * b);
-      #pragma unroll
-      for (int w = 0; w < 2; ++w) {
-        uint32_t word = 0;
-        #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float q = s == 0.f ? 0.f : __fdiv_rn(v[8 * w + e], s);
-          word |= e2m1_code(q) << (4 * e);
-        }
-        packed[2 * b + w] = word;
-      }
-    }
-    uint4* dst = reinterpret_cast<uint4*>(p.packed + ((size_t)l * p.rows + row) * (size_t)(p.k / 2) +
-                                          (size_t)atom * 32);
-    dst[0] = make_uint4(packed[0], packed[1], packed[2], packed[3]);
-    dst[1] = make_uint4(packed[4], packed[5], packed[6], packed[7]);
-    if (p.sf_plain)
-      *reinterpret_cast<uint32_t*>(p.sf_plain + ((size_t)l * p.rows + row) * (size_t)(p.k / 16) +
-                                   (size_t)atom * 4) = sf_word;
-  }
-  // rows past `rows` leave zero scales in the atom's padding
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int sub = lane & 7;                    // which 8 values of the 64-value row segment
   uint8_t* atom_base = p.sf_perm + (((size_t)l * p.row_blocks + rb) * p.k_atoms + atom) * 512;
-  *reinterpret_cast<uint32_t*>(atom_base + (i % 32) * 16 + (i / 32) * 4) = sf_word;
+  constexpr int kSteps = 128 / (4 * (kQuantThreads / 32));
+  // all of this thread's loads first (4 x 32 bytes in flight per lane)
+  float v[kSteps][8];
+  #pragma unroll
+  for (int step = 0; step < kSteps; ++step) {
+    const int r = (step * (kQuantThreads / 32) + warp) * 4 + (lane >> 3);
+    const int row = rb * 128 + r;
+    if (row < p.rows) {
+      const float4* src = reinterpret_cast<const float4*>(
+          p.x + ((size_t)l * p.rows + row) * (size_t)p.k + (size_t)atom * 64 + 8 * sub);
+      const float4 f0 = __ldcs(src), f1 = __ldcs(src + 1);
+      v[step][0] = f0.x, v[step][1] = f0.y, v[step][2] = f0.z, v[step][3] = f0.w;
+      v[step][4] = f1.x, v[step][5] = f1.y, v[step][6] = f1.z, v[step][7] = f1.w;
+    } else {
+      #pragma unroll
+      for (int e = 0; e < 8; ++e) v[step][e] = 0.f;
+    }
+  }
+  #pragma unroll
+  for (int step = 0; step < kSteps; ++step) {
+    const int r = (step * (kQuantThreads / 32) + warp) * 4 + (lane >> 3);   // row in the block
+    const int row = rb * 128 + r;
+    const bool valid = row < p.rows;
+    float amax = 0.f;
+    #pragma unroll
+    for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[step][e]));
+    amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));   // the block's other half
+    const __nv_fp8_storage_t s8 =
+        __nv_cvt_float_to_fp8(__fdiv_rn(amax, 6.0f), __NV_SATFINITE, __NV_E4M3);
+    const float s = __half2float(__half(__nv_cvt_fp8_to_halfraw(s8, __NV_E4M3)));
+    float q[8];
+    #pragma unroll
+    for (int e = 0; e < 8; ++e) q[e] = s == 0.f ? 0.f : __fdiv_rn(v[step][e], s);
+    uint32_t word = 0;
+    #pragma unroll
+    for (int e = 0; e < 4; ++e) word |= e2m1x2(q[2 * e], q[2 * e + 1]) << (8 * e);
+    // scale bytes of blocks 0..3 of this row sit in lanes sub = 0, 2, 4, 6
+    const int row_lane0 = lane & ~7;
+    uint32_t sf_word = 0;
+    #pragma unroll
+    for (int b = 0; b < 4; ++b)
+      sf_word |= (__shfl_sync(0xffffffffu, (uint32_t)s8, row_lane0 + 2 * b) & 0xffu) << (8 * b);
+    if (valid) {
+      *reinterpret_cast<uint32_t*>(p.packed + ((size_t)l * p.rows + row) * (size_t)(p.k / 2) +
+                                   (size_t)atom * 32 + 4 * sub) = word;
+      if (sub == 0 && p.sf_plain)
+        *reinterpret_cast<uint32_t*>(p.sf_plain + ((size_t)l * p.rows + row) * (size_t)(p.k / 16) +
+                                     (size_t)atom * 4) = sf_word;
+    }
+    // rows past `rows` leave zero scales in the atom's padding
+    if (sub == 0)
+      *reinterpret_cast<uint32_t*>(atom_base + (r % 32) * 16 + (r / 32) * 4) = valid ? sf_word : 0u;
+  }
 }
 
 }  // namespace nvfp4

@@ -8,7 +8,9 @@ These produce exactly the byte images the reference task hands to a
   reference generators emit raw bit patterns instead
   (nvfp4_dual_gemm/reference.py:113-146); this quantiser is the one the
   benchmark configurations ask for: scale = e4m3_rne(amax/6),
-  value = e2m1_rne(x / scale) saturating at +-6, zero scale -> zero values.
+  value = e2m1_rne(x / scale) saturating at +-6 (a value rounding to zero
+  keeps its sign, as the sm_100 cvt.e2m1x2 conversion does), zero scale ->
+  (+0) zero values.
 * ``swizzle_sf``: [mn, sf_k, l] scales -> the permuted
   [32, 4, ceil(mn/128), 4, ceil(sf_k/4), l] tensor whose memory is the
   sequence of 512-byte atoms the kernels read
@@ -36,13 +38,13 @@ def ceil_div(a: int, b: int) -> int:
 
 
 def e2m1_codes(q: torch.Tensor) -> torch.Tensor:
-    """fp32 -> e2m1 nibble codes (uint8 0..15), nearest-even, saturating."""
+    """fp32 -> e2m1 nibble codes (uint8 0..15), nearest-even, saturating;
+    the sign bit is the input's sign bit (also for zero)."""
     a = q.abs()
     code = torch.zeros(q.shape, dtype=torch.uint8, device=q.device)
     for bound, inclusive in _E2M1_BOUNDS:
         code += (a >= bound if inclusive else a > bound).to(torch.uint8)
-    neg = torch.signbit(q) & (code != 0)
-    return code | (neg.to(torch.uint8) << 3)
+    return code | (torch.signbit(q).to(torch.uint8) << 3)   # zero keeps its sign
 
 
 def e4m3_codes(x: torch.Tensor) -> torch.Tensor:

@@ -14,7 +14,9 @@ import torch
 from . import _lib
 
 
-def quantize(x: torch.Tensor):
+def quantize(x: torch.Tensor, out=None):
+    """Returns (packed, sf, sf_perm).  ``out``: a tuple returned by an
+    earlier call with the same shape, whose storage is reused (no allocation)."""
     if x.dim() == 2:
         x = x.unsqueeze(0)
     if x.dim() != 3 or x.dtype != torch.float32 or not x.is_cuda:
@@ -25,9 +27,19 @@ def quantize(x: torch.Tensor):
         raise ValueError(f"K={k} must be a multiple of 64")
     rb, ka = -(-rows // 128), k // 64
     dev = x.device
-    packed = torch.empty((l, rows, k // 2), dtype=torch.uint8, device=dev)
-    sf = torch.empty((l, rows, k // 16), dtype=torch.uint8, device=dev)
-    sf_perm = torch.empty((l, rb, ka, 32, 4, 4), dtype=torch.uint8, device=dev)
+    if out is not None:
+        packed = out[0].view(torch.uint8).permute(2, 0, 1)
+        sf = out[1].view(torch.uint8).permute(2, 0, 1)
+        sf_perm = out[2].view(torch.uint8).permute(5, 2, 4, 0, 1, 3)
+        if (tuple(packed.shape) != (l, rows, k // 2) or tuple(sf.shape) != (l, rows, k // 16)
+                or tuple(sf_perm.shape) != (l, rb, ka, 32, 4, 4) or not packed.is_contiguous()
+                or not sf.is_contiguous() or not sf_perm.is_contiguous()
+                or any(t.device != dev for t in (packed, sf, sf_perm))):
+            raise ValueError("out does not match x: pass the tuple an earlier call returned")
+    else:
+        packed = torch.empty((l, rows, k // 2), dtype=torch.uint8, device=dev)
+        sf = torch.empty((l, rows, k // 16), dtype=torch.uint8, device=dev)
+        sf_perm = torch.empty((l, rb, ka, 32, 4, 4), dtype=torch.uint8, device=dev)
     lib = _lib.load()
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream

@@ -63,6 +63,20 @@ def test_quantize_feeds_dual_gemm():
     assert O.allclose_report(out, want, 1e-2, 1e-2)[0] == 0
 
 
+def test_quantize_reuses_out():
+    g = torch.Generator().manual_seed(3)
+    x1 = torch.randn(200, 512, generator=g).cuda()
+    x2 = torch.randn(200, 512, generator=g).cuda()
+    first = quantize(x1)
+    ptrs = [t.data_ptr() for t in first]
+    again = quantize(x2, out=first)
+    assert [t.data_ptr() for t in again] == ptrs
+    fresh = quantize(x2)
+    assert all(torch.equal(a.view(torch.uint8), b.view(torch.uint8)) for a, b in zip(again, fresh))
+    with pytest.raises(ValueError):
+        quantize(torch.randn(128, 512).cuda(), out=first)
+
+
 def test_quantize_rejects_bad_k():
     with pytest.raises(ValueError):
         quantize(torch.zeros(4, 100, device="cuda"))
