@@ -1,6 +1,7 @@
 """Benchmark of the NVFP4 hot paths on B200; prints ONE JSON line (rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+    python bench.py --suite task     # the reference's task.yml shapes vs its published geomeans
 
 Default workload: configuration 1 (dual GEMM M=8192 N=14336 K=4096, the
 compute-bound SiLU-gated FFN shape).  A step is one dual-GEMM call over one
@@ -96,7 +97,7 @@ def group_workload(cfg: int, rank: int, world: int, device):
 
 def quant_workload(rank, world, device):
     """Configuration 5: quantise configuration 1's fp32 operands (A, B1, B2)
-    to NVFP4 on the device; HBM-bound."""
+    to NVFP4 on the device (the producer step in front of both GEMMs); HBM-bound."""
     from nvfp4_b200 import inputs as I
     spec = I.DUAL_CONFIGS[1]
     m, n, k = spec["m"], spec["n"], spec["k"]
@@ -289,6 +290,96 @@ def load_traffic(workload: str):
     return None
 
 
+# ---------------------------------------------------------------------------
+# the reference's own benchmark shapes (task.yml) through custom_kernel
+# ---------------------------------------------------------------------------
+# nvfp4_dual_gemm/task.yml:58-62 and nvfp4_group_gemm/task.yml:59-63 (seed 1111);
+# published geomeans: nvfp4_dual_gemm/README.md:19 (submission_v4) and
+# nvfp4_group_gemm/README.md:33 (submission_v7), both on one B200.
+TASK_DUAL = [(256, 4096, 7168), (512, 4096, 7168), (256, 3072, 4096), (512, 3072, 7168)]
+TASK_GROUP = [([80, 176, 128, 72, 64, 248, 96, 160], 4096, 7168),
+              ([40, 76, 168, 72, 164, 148, 196, 160], 7168, 2048),
+              ([192, 320], 3072, 4096),
+              ([128, 384], 4096, 1536)]
+TASK_PUBLISHED_US = {"dual": 20.692, "group": 25.407}
+TASK_SEED = 1111
+TASK_INPUTS = 15        # distinct inputs per shape, as the reference's eval.py times them
+
+
+def task_inputs(kind, shape, device):
+    """The 15 inputs eval.py builds per benchmark (seed += 42 before each)."""
+    from nvfp4_b200 import inputs as I
+    out = []
+    for i in range(TASK_INPUTS):
+        seed = TASK_SEED + 42 * (i + 1)
+        if kind == "dual":
+            m, n, k = shape
+            out.append(I.generate_dual_input(m, n, k, 1, seed, device=device))
+        else:
+            ms, n, k = shape
+            out.append(I.generate_group_input(ms, [n] * len(ms), [k] * len(ms), len(ms), seed,
+                                              device=device))
+    return out
+
+
+def task_flop(kind, shape):
+    if kind == "dual":
+        m, n, k = shape
+        return 4.0 * m * n * k
+    ms, n, k = shape
+    return sum(2.0 * m * n * k for m in ms)
+
+
+def run_task_suite(args):
+    """Per reference benchmark shape: L2 flushed, then the 15 distinct inputs
+    run back to back between two CUDA events; the per-call mean of `steps`
+    such batches.  One JSON line per task: geomean us against the published
+    geomean of the reference's best submission."""
+    from nvfp4_b200 import _lib
+    from nvfp4_b200.dual_gemm import custom_kernel as dual_kernel
+    from nvfp4_b200.group_gemm import custom_kernel as group_kernel
+    torch.cuda.set_device(0)
+    device = torch.device("cuda", 0)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    for kind, shapes, fn in (("dual", TASK_DUAL, dual_kernel), ("group", TASK_GROUP, group_kernel)):
+        per_shape, tflops = [], []
+        with ClockSampler(0) as clk:
+            for shape in shapes:
+                datas = task_inputs(kind, shape, device)
+                for _ in range(args.warmup):
+                    for d in datas:
+                        fn(d)
+                torch.cuda.synchronize()
+                times = []
+                for _ in range(args.steps):
+                    flush.zero_()
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    for d in datas:
+                        fn(d)
+                    e1.record()
+                    torch.cuda.synchronize()
+                    times.append(e0.elapsed_time(e1) * 1e3 / len(datas))
+                us = statistics.mean(times)
+                per_shape.append(round(us, 3))
+                tflops.append(round(task_flop(kind, shape) / us / 1e6, 1))
+                del datas
+        assert _lib.device_status() == 0
+        geo = float(np.exp(np.mean(np.log(per_shape))))
+        pub = TASK_PUBLISHED_US[kind]
+        print(json.dumps({
+            "metric": f"runtime geomean over the reference's task.yml benchmark shapes "
+                      f"({'dual' if kind == 'dual' else 'grouped'} GEMM)",
+            "value": round(geo, 3), "unit": "us", "higher_is_better": False,
+            "vs_baseline": round(geo / pub, 4), "reference_published_us": pub,
+            "per_shape_us": per_shape, "per_shape_tflops": tflops,
+            "shapes": [list(s) if kind == "dual" else [s[0], s[1], s[2]] for s in shapes],
+            "method": f"{TASK_INPUTS} distinct seeded inputs per shape (reference generator "
+                      f"distributions), L2 flushed before each batch, mean per call over "
+                      f"{args.steps} batches, custom_kernel API",
+            "n_gpus": 1, "clocks": clk.summary()}), flush=True)
+
+
 def metric_name(cfg):
     if cfg == 5:
         return "NVFP4 quantisation bandwidth (fp32 -> e2m1 + e4m3 scales)"
@@ -309,6 +400,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--kernel-only", action="store_true",
                     help="device-timed calls only (no e2e, no CPU baseline): the profiling run")
+    ap.add_argument("--suite", default=None, choices=["task"],
+                    help="task: the reference's own task.yml benchmark shapes, one line per task")
     args = ap.parse_args()
     assert args.warmup >= 3 or args.impl == "reference", "need >= 3 warm-up steps"
 
@@ -319,6 +412,8 @@ def main():
 
     if args.impl == "reference":
         return run_reference_arm(args, cfg, rank, world)
+    if args.suite == "task":
+        return run_task_suite(args)
 
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)

@@ -423,6 +423,7 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   p.sfb2 = static_cast<const uint8_t*>(sfb2);
   p.c = static_cast<__half*>(c);
   p.m = m, p.n = n, p.k = k, p.l = l;
+  p.c_lines32 = (n % 16 == 0) && (reinterpret_cast<uintptr_t>(c) % 32 == 0);
   p.m_blocks = (m + kBM - 1) / kBM;
   p.k_blocks = k / kBK;
   p.group_m = env_int("NVFP4_DUAL_GROUP_M", 16);
@@ -637,6 +638,7 @@ extern "C" int nvfp4_dual_gemm_noalloc(const void* a, const void* b1, const void
   p.sfb2 = static_cast<const uint8_t*>(sfb2);
   p.c = static_cast<__half*>(c);
   p.m = m, p.n = n, p.k = k, p.l = l;
+  p.c_lines32 = (n % 16 == 0) && (reinterpret_cast<uintptr_t>(c) % 32 == 0);
   p.m_blocks = (m + kBM - 1) / kBM;
   p.n_blocks = (n + kBN - 1) / kBN;
   p.k_blocks = k / kBK;

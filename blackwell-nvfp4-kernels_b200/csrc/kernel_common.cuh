@@ -105,4 +105,40 @@ __device__ __forceinline__ void store_lines_coalesced(uint32_t (&w)[32], __half*
   }
 }
 
+__device__ __forceinline__ void st_global_v8(void* p, const uint32_t* w) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(w[0]),
+               "r"(w[1]), "r"(w[2]), "r"(w[3]), "r"(w[4]), "r"(w[5]), "r"(w[6]), "r"(w[7])
+               : "memory");
+}
+
+// Same contract as store_lines_coalesced with 32-byte stores: a 4 x 4
+// transpose of 32-byte chunks inside each group of four lanes, then each of
+// four st.global.v8 writes eight whole 128-byte lines per warp.  Every row
+// start must be 32-byte aligned (ld % 16 == 0 and c_line0 32-byte aligned)
+// and cols_left a multiple of 16 when it is below 64.
+__device__ __forceinline__ void store_lines_coalesced_v8(uint32_t (&w)[32], __half* c_line0,
+                                                         size_t ld, int rows_left, int cols_left) {
+  const int lane = (int)(threadIdx.x & 31u);
+  const int i = lane & 3, grp = lane >> 2;
+  #pragma unroll
+  for (int s = 1; s < 4; s <<= 1) {
+    const bool hi = (i & s) != 0;
+    #pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      if (c & s) continue;           // pair (c, c | s)
+      #pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const uint32_t send = hi ? w[8 * c + e] : w[8 * (c | s) + e];
+        const uint32_t recv = __shfl_xor_sync(0xffffffffu, send, s);
+        if (hi) w[8 * c + e] = recv; else w[8 * (c | s) + e] = recv;
+      }
+    }
+  }
+  #pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const int r = 4 * grp + c;
+    if (r < rows_left && 16 * i < cols_left) st_global_v8(c_line0 + (size_t)r * ld + 16 * i, &w[8 * c]);
+  }
+}
+
 }  // namespace nvfp4

@@ -1,6 +1,6 @@
 // Inline-PTX layer for sm_100a: mbarriers with bounded waits, TMA tile and
 // bulk loads (no cluster multicast anywhere), and the tcgen05 family
-// (TMEM alloc, tcgen05.cp of scale factors, block-scaled MMA, commit, ld).
+// (TMEM alloc, tcgen05.cp of scale factors, block-scaled MMA, commit, ld, st).
 //
 // Descriptor bit layouts follow the PTX ISA "tcgen05 shared memory
 // descriptor" and "instruction descriptor (kind::mxf4nvf4)" tables.
@@ -19,6 +19,7 @@ enum : unsigned {
   kDevTimeoutAccFull  = 1u << 2,   // epilogue waited too long for accumulators
   kDevTimeoutAccFree  = 1u << 3,   // MMA issuer waited too long for TMEM
   kDevTimeoutSelftest = 1u << 4,   // the wait self-test ran out (expected)
+  kDevTimeoutScales   = 1u << 5,   // MMA issuer waited too long for staged scales
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -236,6 +237,44 @@ __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)
 
 __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Register -> TMEM stores of the calling warp's 32-lane quadrant: thread i
+// writes its registers to lane (quadrant base + i), consecutive columns.
+__device__ __forceinline__ void tmem_st_32x32b_x16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_st_32x32b_x32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]),
+      "r"(r[8]), "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]),
+      "r"(r[16]), "r"(r[17]), "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]),
+      "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]),
+      "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+
+// Wait until this thread's tcgen05.st stores have been performed.
+__device__ __forceinline__ void tmem_st_wait() {
+  asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ uint4 lds_v4(uint32_t saddr) {
+  uint4 v;
+  asm volatile("ld.shared.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "r"(saddr)
+               : "memory");
+  return v;
 }
 
 // tcgen05.ld writes its destination registers asynchronously; their values
