@@ -367,7 +367,7 @@ int launch_grouped_chunk(DeviceState* d, int slot, const nvfp4_group* gs, const 
     gi.m_blocks = (g.m + kBM - 1) / kBM;
     gi.n_blocks = (g.n + kBN - 1) / kBN;
     gi.tile_start = tiles;
-    gi.pad_ = 0;
+    gi.lines32 = (g.n % 16 == 0) && (reinterpret_cast<uintptr_t>(g.c) % 32 == 0);
     tiles += g.l * gi.m_blocks * gi.n_blocks;
     if ((rc = encode_operand(&p.tmap_a[i], g.a, g.m, g.k, g.l, kBM))) return rc;
     if ((rc = encode_operand(&p.tmap_b[i], g.b, g.n, g.k, g.l, kBN))) return rc;

@@ -18,8 +18,11 @@
 // * 128x256 tiles (one N=256 MMA per 64-K step, one accumulator buffer whose
 //   columns the epilogue pulls into registers before releasing it) or
 //   128x128 tiles (two accumulator buffers, so the epilogue of one tile
-//   overlaps the MMAs of the next); the scale-factor TMEM region is
-//   double-buffered across stages; empty groups are compacted out on the host.
+//   overlaps the MMAs of the next); empty groups are compacted out on the host;
+// * scale factors reach TMEM as in the dual kernel: they land on their own
+//   mbarrier and four staging warps (one per TMEM lane quadrant) write each
+//   stage's atoms with tcgen05.st into that stage's TMEM scale buffer, so
+//   the tensor pipe runs MMAs only (a tcgen05.cp costs it ~50 cycles).
 #pragma once
 #include <cuda.h>
 #include "kernel_common.cuh"
@@ -31,7 +34,8 @@ struct GroupInfo {
   const uint8_t* sfb;   // [L][ceil(N/128)][K/64][512]
   __half* c;            // [L][M][N]
   int m, n, k, l;
-  int m_blocks, n_blocks, tile_start, pad_;
+  int m_blocks, n_blocks, tile_start;
+  int lines32;          // C rows start 32-byte aligned (N % 16 == 0, C 32-byte aligned)
 };
 
 template <int kMaxGroups>
@@ -51,15 +55,16 @@ struct GroupedCfg {
   static constexpr int kSfbAtoms = kBN / 128;                  // 128-row scale atoms per tile
   static constexpr int kSfbBytes = kSfbAtoms * kSfStageBytes;
   static constexpr int kStageBytes = kABytes + kBBytes + kSfStageBytes + kSfbBytes;
-  static constexpr int kThreads = 32 * (kEpiWarps + 2);
+  static constexpr int kSfWarps = 4;                           // one per TMEM lane quadrant
+  static constexpr int kThreads = 32 * (kEpiWarps + 2 + kSfWarps);
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024;
   static constexpr int kTmemCols = 512;
   static constexpr int kSfCol = kAccBufs * kBN;
-  static constexpr int kSfBufCols = 16 + 16 * kSfbAtoms;       // SFA 4x4 + SFB 4x(4*atoms)
+  static constexpr int kSfBufCols = 16 + 16 * kSfbAtoms;       // SFA 4x4 + SFB 4x(4*atoms), per stage
   static constexpr int kColsPerWarp = kBN / (kEpiWarps / 4);
   static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned");
-  static_assert(kSfCol + 2 * kSfBufCols <= kTmemCols, "TMEM budget");
-  static_assert(kSfCol % 4 == 0 && kSfBufCols % 4 == 0, "tcgen05.cp needs 4-column alignment");
+  static_assert(kSfCol + kStages * kSfBufCols <= kTmemCols, "TMEM budget: one scale buffer per stage");
+  static_assert(kSfCol % 4 == 0 && kSfBufCols % 4 == 0, "scale columns stay 4-aligned");
   static_assert(kBN == 128 || kBN == 256, "tile N");
   static_assert(kEpiWarps % 4 == 0 && kColsPerWarp % 32 == 0, "epilogue split");
 };
@@ -91,6 +96,7 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
   using Cfg = GroupedCfg<kBN, kStages, kEpiWarps, kAccBufs>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_full[kStages], bar_empty[kStages];
+  __shared__ uint64_t bar_sf_landed[kStages], bar_sf_full[kStages];
   __shared__ uint64_t bar_acc_full[kAccBufs], bar_acc_empty[kAccBufs];
   __shared__ uint64_t bar_drain;
   __shared__ uint32_t s_tmem_base;
@@ -105,6 +111,8 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&bar_full[s]), 1);
       mbar_init(smem_u32(&bar_empty[s]), 1);
+      mbar_init(smem_u32(&bar_sf_landed[s]), 1);
+      mbar_init(smem_u32(&bar_sf_full[s]), Cfg::kSfWarps);
     }
     for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(smem_u32(&bar_acc_full[b]), 1);
@@ -155,22 +163,25 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
             break;
           }
           const uint32_t full = smem_u32(&bar_full[stage]);
+          const uint32_t landed = smem_u32(&bar_sf_landed[stage]);
           const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
           const uint32_t sb = sa + Cfg::kABytes;
           const uint32_t ssf = sb + Cfg::kBBytes;
-          mbar_arrive_expect_tx(full, Cfg::kStageBytes);
-          tma_load_3d(sa, &p.tmap_a[tc.g], full, kb * 128, tc.mb * kBM, tc.l, pol);
-          tma_load_3d(sb, &p.tmap_b[tc.g], full, kb * 128, n0, tc.l, pol);
+          // scales first, on their own barrier (staged while the tiles land)
+          mbar_arrive_expect_tx(landed, kSfStageBytes + Cfg::kSfbBytes);
           const size_t sf_off = (size_t)kb * kSfStageBytes;
-          bulk_load(ssf, sfa_t + sf_off, kSfStageBytes, full, pol);
+          bulk_load(ssf, sfa_t + sf_off, kSfStageBytes, landed, pol);
           #pragma unroll
           for (int a = 0; a < Cfg::kSfbAtoms; ++a) {
             // consecutive 128-row atom blocks; a block past N (rows that are
             // never stored) re-reads the last real block instead
             const int blk = min(n0 / 128 + a, n_atoms - 1) - n0 / 128;
             bulk_load(ssf + (1 + a) * kSfStageBytes,
-                      sfb_t + blk * (size_t)rest_k * kSfAtom + sf_off, kSfStageBytes, full, pol);
+                      sfb_t + blk * (size_t)rest_k * kSfAtom + sf_off, kSfStageBytes, landed, pol);
           }
+          mbar_arrive_expect_tx(full, Cfg::kABytes + Cfg::kBBytes);
+          tma_load_3d(sa, &p.tmap_a[tc.g], full, kb * 128, tc.mb * kBM, tc.l, pol);
+          tma_load_3d(sb, &p.tmap_b[tc.g], full, kb * 128, n0, tc.l, pol);
           issued[stage] = true;
           last_phase[stage] = phase;
           if (++stage == kStages) stage = 0, phase ^= 1u;
@@ -178,7 +189,10 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
       }
       if (!ok) {
         for (int s = 0; s < kStages; ++s)
-          if (issued[s]) ctl.drain(smem_u32(&bar_full[s]), last_phase[s]);
+          if (issued[s]) {
+            ctl.drain(smem_u32(&bar_sf_landed[s]), last_phase[s]);
+            ctl.drain(smem_u32(&bar_full[s]), last_phase[s]);
+          }
       }
     }
   } else if (warp == kMma) {
@@ -189,7 +203,6 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
       uint32_t phase = 0;
       int acc = 0;
       uint32_t acc_phase = 0;
-      uint32_t sf_buf = 0;
       bool ok = true, any = false;
       for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
         const GTile tc = grouped_tile(p, t);
@@ -201,32 +214,25 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
         tc_fence_after();
         const uint32_t d = tmem + acc * kBN;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!ctl.wait(smem_u32(&bar_full[stage]), phase, kDevTimeoutTmaFull)) {
+          // operand tiles landed, and the stage's scales staged into TMEM
+          if (!ctl.wait(smem_u32(&bar_full[stage]), phase, kDevTimeoutTmaFull) ||
+              !ctl.wait(smem_u32(&bar_sf_full[stage]), phase, kDevTimeoutScales)) {
             ok = false;
             break;
           }
           tc_fence_after();
           const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
           const uint32_t sb = sa + Cfg::kABytes;
-          const uint32_t ssf = sb + Cfg::kBBytes;
-          const uint32_t sf_a = tmem + Cfg::kSfCol + sf_buf * Cfg::kSfBufCols;
+          // scales of k-step j: SFA in [sf_a+4j, +4), SFB atom a in [sf_b+4(atoms*j+a), +4)
+          const uint32_t sf_a = tmem + Cfg::kSfCol + stage * Cfg::kSfBufCols;
           const uint32_t sf_b = sf_a + 16;
-          #pragma unroll
-          for (int j = 0; j < kBK / kKStep; ++j) {
-            tc_cp_sf_atom(sf_a + 4 * j, sf_atom_desc(ssf + j * kSfAtom));
-            #pragma unroll
-            for (int a = 0; a < Cfg::kSfbAtoms; ++a)
-              tc_cp_sf_atom(sf_b + 4 * (Cfg::kSfbAtoms * j + a),
-                            sf_atom_desc(ssf + (1 + a) * kSfStageBytes + j * kSfAtom));
-          }
           #pragma unroll
           for (int j = 0; j < kBK / kKStep; ++j) {
             tc_mma_nvf4(d, kmajor_sw128_desc(sa + 32 * j), kmajor_sw128_desc(sb + 32 * j), idesc,
                         sf_a + 4 * j, sf_b + 4 * Cfg::kSfbAtoms * j, (kb | j) != 0);
           }
-          tc_commit(smem_u32(&bar_empty[stage]));
+          tc_commit(smem_u32(&bar_empty[stage]));   // frees the stage and its scale buffer
           any = true;
-          sf_buf ^= 1u;
           if (++stage == kStages) stage = 0, phase ^= 1u;
         }
         if (!ok) break;
@@ -236,6 +242,52 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
       if (!ok && any) {
         tc_commit(smem_u32(&bar_drain));
         ctl.drain(smem_u32(&bar_drain), 0);
+      }
+    }
+  } else if (warp >= kEpiWarps + 2) {
+    // ------------------------------------------------------------ scale staging
+    // Warp w writes TMEM lanes [32*(w%4), +32); lane i of every quadrant gets
+    // row i of each 512-byte atom (the broadcast image the MMA reads: tile row
+    // r's scales at lane r, column base + r/32).
+    const uint32_t t_quad = ((uint32_t)(warp & 3) * 32u) << 16;
+    constexpr int kSfbRegs = 16 * Cfg::kSfbAtoms;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
+      const GTile tc = grouped_tile(p, t);
+      const int k_blocks = p.g[tc.g].k / kBK;
+      for (int kb = 0; kb < k_blocks; ++kb) {
+        bool got = true;
+        if (lane == 0) got = ctl.wait(smem_u32(&bar_sf_landed[stage]), phase, kDevTimeoutTmaFull);
+        if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) {
+          ok = false;
+          break;
+        }
+        mbar_try_wait(smem_u32(&bar_sf_landed[stage]), phase);   // every lane observes the phase
+        const uint32_t ssf = smem_base + stage * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes +
+                             lane * 16u;
+        uint32_t ra[16], rb[kSfbRegs];
+        #pragma unroll
+        for (int j = 0; j < kBK / kKStep; ++j) {
+          const uint4 v = lds_v4(ssf + j * kSfAtom);
+          ra[4 * j + 0] = v.x, ra[4 * j + 1] = v.y, ra[4 * j + 2] = v.z, ra[4 * j + 3] = v.w;
+          #pragma unroll
+          for (int a = 0; a < Cfg::kSfbAtoms; ++a) {
+            const uint4 b = lds_v4(ssf + (1 + a) * kSfStageBytes + j * kSfAtom);
+            const int o = 4 * (Cfg::kSfbAtoms * j + a);
+            rb[o + 0] = b.x, rb[o + 1] = b.y, rb[o + 2] = b.z, rb[o + 3] = b.w;
+          }
+        }
+        const uint32_t t_buf = tmem + t_quad + Cfg::kSfCol + stage * Cfg::kSfBufCols;
+        tmem_st_32x32b_x16(t_buf, ra);
+        if constexpr (Cfg::kSfbAtoms == 2) tmem_st_32x32b_x32(t_buf + 16, rb);
+        else tmem_st_32x32b_x16(t_buf + 16, rb);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bar_sf_full[stage]));
+        if (++stage == kStages) stage = 0, phase ^= 1u;
       }
     }
   } else {
@@ -255,39 +307,50 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
       const int row0 = tc.mb * kBM + quad * 32;
       const int col0 = tc.nb * kBN + part * kCW;
       __half* cl0 = gi.c + ((size_t)tc.l * gi.m + row0) * (size_t)gi.n + col0;
-      // one 64-column (128-byte) line per lane at a time
-      auto store_line = [&](const uint32_t (&lo)[32], const uint32_t (&hi)[32], int line) {
-        uint32_t w[32];
+      // fp16 words of one 64-column (128-byte) line per lane -> whole-line stores
+      auto pack_line = [&](uint32_t (&w)[32], const uint32_t (&lo)[32], const uint32_t (&hi)[32]) {
         #pragma unroll
         for (int e = 0; e < 16; ++e) {
           w[e] = pack_half2(__uint_as_float(lo[2 * e]), __uint_as_float(lo[2 * e + 1]));
           w[16 + e] = pack_half2(__uint_as_float(hi[2 * e]), __uint_as_float(hi[2 * e + 1]));
         }
-        store_lines_coalesced(w, cl0 + 64 * line, gi.n, gi.m - row0, gi.n - col0 - 64 * line);
+      };
+      auto store_line = [&](uint32_t (&w)[32], int line) {
+        if (gi.lines32)
+          store_lines_coalesced_v8(w, cl0 + 64 * line, gi.n, gi.m - row0, gi.n - col0 - 64 * line);
+        else
+          store_lines_coalesced(w, cl0 + 64 * line, gi.n, gi.m - row0, gi.n - col0 - 64 * line);
       };
       if constexpr (kAccBufs == 1) {
-        // pull the whole slice into registers, hand TMEM back, then store
-        uint32_t v[kChunks][32];
+        // pull the whole slice into registers, hand TMEM back, pack to fp16
+        // (halving the live registers), then store
+        uint32_t w[kChunks / 2][32];
+        {
+          uint32_t v[kChunks][32];
+          #pragma unroll
+          for (int c = 0; c < kChunks; ++c) tmem_ld_32x32b_x32(t_acc + 32 * c, v[c]);
+          tmem_ld_wait();
+          #pragma unroll
+          for (int c = 0; c < kChunks; ++c) tmem_regs_ready(v[c]);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[acc]));
+          #pragma unroll
+          for (int c = 0; c < kChunks; c += 2) pack_line(w[c / 2], v[c], v[c + 1]);
+        }
         #pragma unroll
-        for (int c = 0; c < kChunks; ++c) tmem_ld_32x32b_x32(t_acc + 32 * c, v[c]);
-        tmem_ld_wait();
-        #pragma unroll
-        for (int c = 0; c < kChunks; ++c) tmem_regs_ready(v[c]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[acc]));
-        #pragma unroll
-        for (int c = 0; c < kChunks; c += 2) store_line(v[c], v[c + 1], c / 2);
+        for (int ln = 0; ln < kChunks / 2; ++ln) store_line(w[ln], ln);
       } else {
         #pragma unroll 1
         for (int c = 0; c < kChunks; c += 2) {
-          uint32_t lo[32], hi[32];
+          uint32_t lo[32], hi[32], w[32];
           tmem_ld_32x32b_x32(t_acc + 32 * c, lo);
           tmem_ld_32x32b_x32(t_acc + 32 * c + 32, hi);
           tmem_ld_wait();
           tmem_regs_ready(lo);
           tmem_regs_ready(hi);
-          store_line(lo, hi, c / 2);
+          pack_line(w, lo, hi);
+          store_line(w, c / 2);
         }
         tc_fence_before();
         __syncwarp();

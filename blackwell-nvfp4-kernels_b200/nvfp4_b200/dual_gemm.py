@@ -8,6 +8,8 @@ and c; the un-permuted scales are not needed.
 """
 from __future__ import annotations
 
+import weakref
+
 import torch
 
 from . import _lib
@@ -43,8 +45,8 @@ def check_sf_perm(name, t, mn, k, l, device):
     _expect(ok, f"{name}: strides {got} are not the atom layout {want}")
 
 
-def dual_gemm(a, b1, b2, sfa_perm, sfb1_perm, sfb2_perm, c) -> torch.Tensor:
-    """c[:, :, l] = silu(A_l . B1_lᵀ) * (A_l . B2_lᵀ) in fp16, on c's stream."""
+def _validate(a, b1, b2, sfa_perm, sfb1_perm, sfb2_perm, c):
+    """Check every tensor against the task layout; returns (m, n, k, l, device)."""
     _expect(c.dtype == torch.float16, f"c: expected float16, got {c.dtype}")
     _expect(c.is_cuda, "c must be a CUDA tensor")
     m, n, l = c.shape
@@ -59,12 +61,61 @@ def dual_gemm(a, b1, b2, sfa_perm, sfb1_perm, sfb2_perm, c) -> torch.Tensor:
     check_sf_perm("sfb2_permuted", sfb2_perm, n, k, l, dev)
     _expect(c.stride(0) == n and c.stride(1) == 1 and (l == 1 or c.stride(2) == m * n),
             f"c: strides {c.stride()} are not the row-major [L][M][N] layout")
+    return m, n, k, l, dev
+
+
+def on_device(device: torch.device, launch):
+    """Run launch(stream_handle) with `device` current (the library launches
+    on the current device) and its current stream; the device switch is
+    skipped when `device` is current already (the common case)."""
+    if torch.cuda.current_device() == device.index:
+        return launch(torch.cuda.current_stream().cuda_stream)
+    with torch.cuda.device(device):
+        return launch(torch.cuda.current_stream(device).cuda_stream)
+
+
+class _Plan:
+    """A validated call: weak references to the seven tensors the kernel
+    reads or writes, their data pointers, shapes and strides, and the size
+    arguments.  A later call with the same tensor objects, still at the same
+    addresses with the same shapes and strides, skips re-validation."""
+
+    def __init__(self, ts, sizes, device):
+        self.refs = tuple(weakref.ref(t) for t in ts)
+        self.sig = tuple((t.data_ptr(), t.shape, t.stride()) for t in ts)
+        self.ptrs = tuple(s[0] for s in self.sig)
+        self.sizes, self.device = sizes, device
+
+    def matches(self, ts) -> bool:
+        for t, r in zip(ts, self.refs):
+            if t is not r():
+                return False
+        return tuple((t.data_ptr(), t.shape, t.stride()) for t in ts) == self.sig
+
+
+_PLAN_SLOTS = 64        # >= the 15 rotating inputs of the reference's timing loop
+_plans: dict = {}
+
+
+def clear_plan_cache() -> None:
+    _plans.clear()
+
+
+def dual_gemm(a, b1, b2, sfa_perm, sfb1_perm, sfb2_perm, c) -> torch.Tensor:
+    """c[:, :, l] = silu(A_l . B1_lᵀ) * (A_l . B2_lᵀ) in fp16, on c's stream."""
+    ts = (a, b1, b2, sfa_perm, sfb1_perm, sfb2_perm, c)
+    key = tuple(id(t) for t in ts)
+    plan = _plans.get(key)
+    if plan is None or not plan.matches(ts):
+        m, n, k, l, dev = _validate(*ts)
+        plan = _Plan(ts, (m, n, k, l), dev)
+        if len(_plans) >= _PLAN_SLOTS:
+            _plans.pop(next(iter(_plans)))
+        _plans[key] = plan
+    m, n, k, l = plan.sizes
     lib = _lib.load()
-    with torch.cuda.device(dev):
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        _lib.check(lib.nvfp4_dual_gemm(
-            a.data_ptr(), b1.data_ptr(), b2.data_ptr(), sfa_perm.data_ptr(),
-            sfb1_perm.data_ptr(), sfb2_perm.data_ptr(), c.data_ptr(), m, n, k, l, stream))
+    _lib.check(on_device(plan.device,
+                         lambda st: lib.nvfp4_dual_gemm(*plan.ptrs, m, n, k, l, st)))
     return c
 
 

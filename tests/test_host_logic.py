@@ -52,6 +52,38 @@ def test_plan_holds_no_strong_references():
     assert plan.refs[0][0]() is None
 
 
+def _dual_tensors(m=128, n=128, k=256):
+    d = I.generate_dual_input(m, n, k, 1, seed=5, device="cpu")
+    return (d[0], d[1], d[2], d[6], d[7], d[8], d[9])
+
+
+def test_dual_plan_matches_same_objects_only():
+    from nvfp4_b200.dual_gemm import _Plan as DualPlan
+    ts = _dual_tensors()
+    plan = DualPlan(ts, (128, 128, 256, 1), device=None)
+    assert plan.matches(ts)
+    assert plan.matches(list(ts))                                       # same tensors, new container
+    assert not plan.matches(ts[:6] + (ts[6].clone(),))                  # a replaced output
+    c = ts[6]
+    c.set_(c.clone())                                                   # same object, new storage
+    assert not plan.matches(ts)
+
+
+def test_dual_plan_detects_restride_and_holds_no_references():
+    import gc
+    import weakref
+    from nvfp4_b200.dual_gemm import _Plan as DualPlan
+    ts = _dual_tensors()
+    plan = DualPlan(ts, (128, 128, 256, 1), device=None)
+    a = ts[0]
+    a.as_strided_(a.shape, (a.stride(0), 1, a.stride(0) * a.shape[0] + 64))   # same storage, new strides
+    assert not plan.matches(ts)
+    probe = weakref.ref(ts[1])
+    del ts, a
+    gc.collect()
+    assert probe() is None
+
+
 @pytest.mark.parametrize("n,world", [(14336, 1), (14336, 2), (14336, 8), (7168, 8), (1000, 3)])
 def test_n_shard_covers_and_aligns(n, world):
     spans = [n_shard(n, world, r) for r in range(world)]
