@@ -10,6 +10,7 @@
 #include <cstdlib>
 #include <cstring>
 #include <mutex>
+#include <unistd.h>
 #include <unordered_map>
 #include <vector>
 
@@ -66,6 +67,7 @@ struct DeviceState {
   int num_sms = 0;
   unsigned* status = nullptr;
   bool smem_set[32] = {};  // one slot per kernel instantiation
+  int max_clusters[5] = {};  // co-resident clusters of the cluster split-K kernel, by size
   std::unordered_map<cudaStream_t, Workspace> ws;
   unsigned char* noalloc_scratch = nullptr;   // device address of g_noalloc_scratch
 };
@@ -86,6 +88,41 @@ long long wait_limit_cycles() {
 int env_int(const char* name, int dflt) {
   const char* e = getenv(name);
   return e ? atoi(e) : dflt;
+}
+
+// Tuning knobs (NVFP4_* environment variables) read in one pass over the
+// environment per call: a getenv per knob costs a full scan each, which at
+// ~1 us of host time per call matters for microsecond-scale problems.  They
+// are re-read on every call so a process can change them between calls.
+struct Knobs {
+  int dual_group_m = 16;   // NVFP4_DUAL_GROUP_M
+  int dual_splits = 0;     // NVFP4_DUAL_SPLITS (0 = automatic)
+  int dual_bn = 0;         // NVFP4_DUAL_BN (64 / 128; 0 = automatic)
+  bool dual_pair = false;  // NVFP4_DUAL_KERNEL=pair
+  int dual_cluster = 0;    // NVFP4_DUAL_CLUSTER: 0 automatic, 1 off, 2 / 4 forced cluster split-K
+  int grouped_bn = 0;      // NVFP4_GROUPED_BN (128 / 256; 0 = automatic)
+};
+
+Knobs read_knobs() {
+  Knobs k;
+  for (char** e = environ; e && *e; ++e) {
+    const char* v = *e;
+    if (strncmp(v, "NVFP4_", 6) != 0) continue;
+    v += 6;
+    auto val = [&](const char* name) -> const char* {
+      const size_t n = strlen(name);
+      return (strncmp(v, name, n) == 0 && v[n] == '=') ? v + n + 1 : nullptr;
+    };
+    const char* x;
+    if ((x = val("DUAL_GROUP_M"))) k.dual_group_m = atoi(x);
+    else if ((x = val("DUAL_SPLITS"))) k.dual_splits = atoi(x);
+    else if ((x = val("DUAL_BN"))) k.dual_bn = atoi(x);
+    else if ((x = val("DUAL_KERNEL"))) k.dual_pair = strcmp(x, "pair") == 0;
+    else if ((x = val("DUAL_CLUSTER"))) k.dual_cluster = atoi(x);
+    else if ((x = val("GROUPED_BN"))) k.grouped_bn = atoi(x);
+  }
+  if (k.dual_group_m < 1) k.dual_group_m = 1;
+  return k;
 }
 
 // Resolve per-device state (SM count, status-word address) once.
@@ -268,10 +305,14 @@ void reset_workspaces(DeviceState* d) {
     if (kv.second.counters) cudaMemset(kv.second.counters, 0, kv.second.counter_count * sizeof(int));
 }
 
-// Number of K splits for the 128-wide dual kernel: enough work units to give
-// every SM one, each split at least two 256-deep K blocks, at most 16.
+// Number of K splits for the 128-wide dual kernel.  A split costs the
+// partial-sum exchange through global memory (~5 us on B200), which measured
+// slower than leaving SMs idle once there are at least a quarter as many
+// tiles as SMs (e.g. 48 tiles: 18.4 us unsplit, 24.6 us in 2 splits, 28.7 us
+// in 3).  Below that: enough work units to give every SM one, each split at
+// least two 256-deep K blocks, at most 16.
 int choose_splits(int tiles, int k_blocks, int num_sms) {
-  if (tiles >= num_sms) return 1;
+  if (4 * tiles >= num_sms) return 1;
   int s = num_sms / tiles;
   s = s < k_blocks / 2 ? s : k_blocks / 2;
   s = s < 16 ? s : 16;
@@ -279,17 +320,89 @@ int choose_splits(int tiles, int k_blocks, int num_sms) {
 }
 
 // ---------------------------------------------------------------- dual GEMM
+// Cluster split-K launch: grid = tiles * S CTAs in clusters of S (one unit
+// per CTA), no workspace.
+template <int kStages, int S>
+int launch_dual_cluster(DeviceState* d, int slot, DualParams& p, cudaStream_t stream) {
+  using Cfg = DualCfg<128, kStages, 8, 1>;
+  auto kern = dual_gemm_kernel<128, kStages, 8, 1, true, S>;
+  int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
+  if (rc) return rc;
+  p.splits = S;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(p.tiles * S), 1, 1);
+  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  if (e != cudaSuccess)
+    return fail(NVFP4_ERR_CUDA, "dual_gemm_kernel (cluster %d) launch: %s", S, cudaGetErrorString(e));
+  return check_launch("dual_gemm_kernel (cluster split-K)");
+}
+
+// How many S-CTA clusters of the cluster split-K kernel fit on the device at
+// once (cached; 0 if the query fails).
+template <int kStages, int S>
+int max_active_clusters(DeviceState* d, int slot) {
+  if (d->max_clusters[S]) return d->max_clusters[S];
+  using Cfg = DualCfg<128, kStages, 8, 1>;
+  auto kern = dual_gemm_kernel<128, kStages, 8, 1, true, S>;
+  if (set_smem_once(d, slot, kern, Cfg::kSmemBytes)) return 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(S * d->num_sms), 1, 1);
+  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = S;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess) {
+    cudaGetLastError();
+    n = 0;
+  }
+  d->max_clusters[S] = n > 0 ? n : -1;
+  return n;
+}
+
 template <int kBN, int kStages, int kEpiWarps, int kAccBufs>
-int launch_dual(DeviceState* d, int slot, DualParams& p, cudaStream_t stream) {
+int launch_dual(DeviceState* d, int slot, DualParams& p, int forced_splits, int cluster,
+                cudaStream_t stream) {
   using Cfg = DualCfg<kBN, kStages, kEpiWarps, kAccBufs>;
   int rc = NVFP4_OK;
   p.n_blocks = (p.n + kBN - 1) / kBN;
   p.tiles = p.l * p.m_blocks * p.n_blocks;
   p.splits = 1;
+  if constexpr (kBN == 128 && kEpiWarps == 8 && kAccBufs == 1) {
+    // Cluster split-K when the tiles leave SMs idle, every split keeps at
+    // least two 256-deep K blocks, and all clusters fit on the device at once
+    // (partials cross the cluster instead of global memory).
+    if (forced_splits < 1 && cluster != 1 && p.tiles < d->num_sms) {
+      const int want = cluster == 2 || cluster == 4 ? cluster
+                       : (4 * p.tiles <= d->num_sms ? 4 : 2);
+      for (int S = want; S >= 2; S /= 2) {
+        if (p.k_blocks < 2 * S) continue;
+        const int fit = S == 4 ? max_active_clusters<kStages, 4>(d, 13)
+                               : max_active_clusters<kStages, 2>(d, 12);
+        if (p.tiles > fit) continue;
+        return S == 4 ? launch_dual_cluster<kStages, 4>(d, 13, p, stream)
+                      : launch_dual_cluster<kStages, 2>(d, 12, p, stream);
+      }
+    }
+  }
   if (kBN == 128) {
     p.splits = choose_splits(p.tiles, p.k_blocks, d->num_sms);
-    const int forced = env_int("NVFP4_DUAL_SPLITS", 0);
-    if (forced >= 1) p.splits = forced < p.k_blocks ? forced : p.k_blocks;
+    if (forced_splits >= 1) p.splits = forced_splits < p.k_blocks ? forced_splits : p.k_blocks;
   }
   if (p.splits > 1) {
     Workspace* w = nullptr;
@@ -317,7 +430,7 @@ int launch_dual(DeviceState* d, int slot, DualParams& p, cudaStream_t stream) {
 template <int kStages>
 int launch_dual_pair(DeviceState* d, int slot, const void* a, const void* b1, const void* b2,
                      const void* sfa, const void* sfb1, const void* sfb2, void* c, int m, int n,
-                     int k, int l, cudaStream_t stream) {
+                     int k, int l, int group_m, cudaStream_t stream) {
   using Cfg = DualPairCfg<kStages>;
   auto kern = dual_gemm_pair_kernel<kStages>;
   int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
@@ -332,8 +445,7 @@ int launch_dual_pair(DeviceState* d, int slot, const void* a, const void* b1, co
   p.tiles = l * p.mp_blocks * p.n_blocks;
   p.sfa_blocks = (m + 127) / 128;
   p.sfb_blocks = (n + 127) / 128;
-  p.group_m = env_int("NVFP4_DUAL_GROUP_M", 16);
-  if (p.group_m < 1) p.group_m = 1;
+  p.group_m = group_m;
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
   if ((rc = encode_operand(&p.tmap_a, a, m, k, l, kBM))) return rc;
@@ -426,8 +538,8 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   p.c_lines32 = (n % 16 == 0) && (reinterpret_cast<uintptr_t>(c) % 32 == 0);
   p.m_blocks = (m + kBM - 1) / kBM;
   p.k_blocks = k / kBK;
-  p.group_m = env_int("NVFP4_DUAL_GROUP_M", 16);
-  if (p.group_m < 1) p.group_m = 1;
+  const Knobs kn = read_knobs();
+  p.group_m = kn.dual_group_m;
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
 
@@ -436,19 +548,18 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   // 30% fewer operand bytes per SM but measures slower on B200: its
   // tcgen05.cp.cta_group::2 scale copies run ~2x longer than the single-CTA
   // copies and serialise with the MMAs in the tensor pipe.
-  const char* kern_env = getenv("NVFP4_DUAL_KERNEL");
-  if (kern_env && strcmp(kern_env, "pair") == 0)
-    return launch_dual_pair<5>(d, 2, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l, stream);
+  if (kn.dual_pair)
+    return launch_dual_pair<5>(d, 2, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l, kn.dual_group_m,
+                               stream);
   // 128-wide tiles (one fused N=256 MMA per K step), split along K when
   // there are fewer tiles than SMs; 64-wide tiles only on request.
   int bn = 128;
-  const int forced = env_int("NVFP4_DUAL_BN", 0);
-  if (forced == 64 || forced == 128) bn = forced;
+  if (kn.dual_bn == 64 || kn.dual_bn == 128) bn = kn.dual_bn;
   if ((rc = encode_operand(&p.tmap_a, a, m, k, l, kBM))) return rc;
   if ((rc = encode_operand(&p.tmap_b1, b1, n, k, l, bn))) return rc;
   if ((rc = encode_operand(&p.tmap_b2, b2, n, k, l, bn))) return rc;
-  if (bn == 128) return launch_dual<128, 4, 8, 1>(d, 0, p, stream);
-  return launch_dual<64, 5, 4, 2>(d, 1, p, stream);
+  if (bn == 128) return launch_dual<128, 4, 8, 1>(d, 0, p, kn.dual_splits, kn.dual_cluster, stream);
+  return launch_dual<64, 5, 4, 2>(d, 1, p, kn.dual_splits, kn.dual_cluster, stream);
 }
 
 extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream_) {
@@ -481,7 +592,7 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
   int min_n = groups[live[0]].n;
   for (int i : live) min_n = groups[i].n < min_n ? groups[i].n : min_n;
   int bn = min_n >= 256 ? 256 : 128;
-  const int forced = env_int("NVFP4_GROUPED_BN", 0);
+  const int forced = read_knobs().grouped_bn;
   if (forced == 128 || forced == 256) bn = forced;
   if (n <= 16) return launch_grouped<16>(d, groups, live.data(), n, bn, stream);
   for (int s = 0; s < n; s += 96) {

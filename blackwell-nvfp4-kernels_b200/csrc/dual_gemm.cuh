@@ -32,10 +32,17 @@
 //   before doing the math and stores, so the next tile's MMAs start early;
 // * the epilogue transposes each warp's 32 rows x 64 fp16 columns through
 //   shuffles so every store instruction writes whole 128-byte lines;
-// * split-K for shapes with too few tiles to fill the GPU: each split's
-//   partial gate/up sums go to an fp32 workspace slot; the split that draws
-//   the last ticket sums the slots in split order and alone applies the SiLU
-//   gate (the epilogue is not linear, so the reduction must finish first).
+// * split-K for shapes with too few tiles to fill the GPU, in two forms.
+//   Cluster split-K (kCluster = 2 or 4): the splits of a tile run as one
+//   thread-block cluster; after the main loop every CTA owns 128/kCluster of
+//   the tile's output columns, the others write their fp32 gate/up partials
+//   for that slice into the owner's (now idle) pipeline shared memory over
+//   the cluster (st.shared::cluster), and the owner sums them in split order
+//   (deterministic), applies the SiLU gate and stores.  Workspace split-K
+//   (kCluster = 0): each split's partials go to an fp32 global workspace
+//   slot; the split that draws the last ticket sums the slots in split order
+//   and alone applies the gate (the epilogue is not linear, so the reduction
+//   must finish first).
 #pragma once
 #include <cuda.h>
 #include "kernel_common.cuh"
@@ -117,15 +124,25 @@ __device__ __forceinline__ KRange dual_unit(const DualParams& p, int u) {
   return r;
 }
 
-template <int kBN, int kStages, int kEpiWarps, int kAccBufs, bool kSplitK>
+template <int kBN, int kStages, int kEpiWarps, int kAccBufs, bool kSplitK, int kCluster = 0>
 __global__ void __launch_bounds__(DualCfg<kBN, kStages, kEpiWarps, kAccBufs>::kThreads, 1)
 dual_gemm_kernel(const __grid_constant__ DualParams p) {
   using Cfg = DualCfg<kBN, kStages, kEpiWarps, kAccBufs>;
+  static_assert(kCluster == 0 || (kSplitK && kBN == 128 && kEpiWarps == 8 &&
+                                  (kCluster == 2 || kCluster == 4)),
+                "cluster split-K: 128-wide tiles, 8 epilogue warps, 2 or 4 splits");
+  // cluster split-K receive buffer in the owner's stage ring: per sending
+  // split, gate and up of the owned 128/kCluster columns, [col][row] fp32
+  constexpr int kOwnCols = kCluster ? 128 / kCluster : 128;
+  constexpr int kRxSlotFloats = 2 * kOwnCols * kBM;
+  static_assert(kCluster == 0 || (kCluster - 1) * kRxSlotFloats * 4 <= kStages * Cfg::kStageBytes,
+                "receive buffer fits the stage ring");
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_full[kStages], bar_empty[kStages];
   __shared__ uint64_t bar_sf_landed[kStages], bar_sf_full[kStages];
   __shared__ uint64_t bar_acc_full[kAccBufs], bar_acc_empty[kAccBufs];
   __shared__ uint64_t bar_drain;
+  __shared__ uint64_t bar_peer_ready, bar_rx_full;   // cluster split-K exchange
   __shared__ uint32_t s_tmem_base;
   __shared__ volatile int s_abort;
   __shared__ volatile int s_ticket, s_fail;   // split-K epilogue decisions (uniform after a barrier)
@@ -147,6 +164,12 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
       mbar_init(smem_u32(&bar_acc_empty[b]), kEpiWarps);
     }
     mbar_init(smem_u32(&bar_drain), 1);
+    if constexpr (kCluster > 0) {
+      mbar_init(smem_u32(&bar_peer_ready), kCluster - 1);        // one arrive per other CTA
+      // every lane of the 4 warps holding an owned column range arrives once
+      // per 32-column chunk it sends, from each of the kCluster-1 other CTAs
+      mbar_init(smem_u32(&bar_rx_full), (kCluster - 1) * 4 * 32 * (kOwnCols / 32));
+    }
     s_abort = 0;
     s_fail = 0;
     fence_barrier_init();
@@ -162,6 +185,7 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
   if (warp == kEpiWarps + 1) tmem_alloc<Cfg::kTmemCols>(smem_u32(&s_tmem_base));
   tc_fence_before();
   __syncthreads();
+  if constexpr (kCluster > 0) cluster_sync();   // peers' barriers exist before any remote arrive
   tc_fence_after();
   const uint32_t tmem = s_tmem_base;
   const AbortCtl ctl{&s_abort, p.status, p.wait_limit};
@@ -364,6 +388,104 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
       tc_fence_after();
       const uint32_t t_gate = tmem + ((uint32_t)(quad * 32) << 16) + acc * Cfg::kAccCols + part * kCW;
       const uint32_t t_up = t_gate + kBN;
+      if constexpr (kCluster > 0) {
+        // ---- cluster split-K: one unit per CTA; this CTA is split `rank`
+        const uint32_t rank = (uint32_t)kr.split;
+        // this CTA's pipeline is drained: its stage ring may now receive
+        if (et == 0)
+          for (uint32_t o = 0; o < (uint32_t)kCluster; ++o)
+            if (o != rank) mbar_arrive_cluster(mapa_shared(smem_u32(&bar_peer_ready), o));
+        bool ok = true;
+        if (lane == 0) ok = ctl.wait_cluster(smem_u32(&bar_peer_ready), 0, kDevTimeoutPeers);
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+        if (!ok) break;
+        mbar_try_wait_cluster(smem_u32(&bar_peer_ready), 0);
+        // send the 32-column chunks other CTAs own ([gate|up][col][row] in
+        // slot (rank < owner ? rank : rank - 1) of the owner's buffer)
+        #pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int tcol = part * kCW + 32 * c;          // tile column of the chunk
+          const uint32_t owner = (uint32_t)(tcol / kOwnCols);
+          if (owner == rank) continue;
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(t_gate + 32 * c, g);
+          tmem_ld_32x32b_x32(t_up + 32 * c, u);
+          tmem_ld_wait();
+          tmem_regs_ready(g), tmem_regs_ready(u);
+          const uint32_t slot = rank < owner ? rank : rank - 1;
+          const uint32_t rx = mapa_shared(smem_base, owner) +
+                              4u * (slot * kRxSlotFloats + (uint32_t)(tcol - owner * kOwnCols) * kBM +
+                                    (uint32_t)trow);
+          #pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            st_shared_cluster_f32(rx + 4u * i * kBM, __uint_as_float(g[i]));
+            st_shared_cluster_f32(rx + 4u * (kOwnCols + i) * kBM, __uint_as_float(u[i]));
+          }
+          mbar_arrive_cluster(mapa_shared(smem_u32(&bar_rx_full), owner));   // release: the stores above
+        }
+        // reduce the chunk(s) this CTA owns: splits in order 0..kCluster-1
+        uint32_t w[32];
+        int own_c0 = -1, own_n = 0;
+        #pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int tcol = part * kCW + 32 * c;
+          if ((uint32_t)(tcol / kOwnCols) != rank) continue;
+          if (own_c0 < 0) {
+            own_c0 = c;
+            bool got_rx = true;
+            if (lane == 0) got_rx = ctl.wait_cluster(smem_u32(&bar_rx_full), 0, kDevTimeoutPeers);
+            if (!__shfl_sync(0xffffffffu, got_rx ? 1 : 0, 0)) { ok = false; break; }
+            mbar_try_wait_cluster(smem_u32(&bar_rx_full), 0);
+          }
+          uint32_t g[32], u[32];
+          tmem_ld_32x32b_x32(t_gate + 32 * c, g);
+          tmem_ld_32x32b_x32(t_up + 32 * c, u);
+          tmem_ld_wait();
+          tmem_regs_ready(g), tmem_regs_ready(u);
+          const float* rxl = reinterpret_cast<const float*>(smem_raw + (smem_base - smem_u32(smem_raw))) +
+                             (tcol - (int)rank * kOwnCols) * kBM + trow;
+          #pragma unroll
+          for (int e = 0; e < 16; ++e) {
+            float gs[2], us[2];
+            #pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const int i = 2 * e + h;
+              float ga = 0.f, ua = 0.f;
+              #pragma unroll
+              for (int sp = 0; sp < kCluster; ++sp) {
+                if (sp == (int)rank) {
+                  ga += __uint_as_float(g[i]);
+                  ua += __uint_as_float(u[i]);
+                } else {
+                  const float* slot = rxl + (sp < (int)rank ? sp : sp - 1) * kRxSlotFloats;
+                  ga += slot[i * kBM];
+                  ua += slot[(kOwnCols + i) * kBM];
+                }
+              }
+              gs[h] = ga, us[h] = ua;
+            }
+            // owned chunks: both (2 splits, slot 16c) or one (4 splits, slot 0)
+            w[(kOwnCols == 64 ? 16 * c : 0) + e] = pack_half2(silu_gate(gs[0], us[0]), silu_gate(gs[1], us[1]));
+          }
+          ++own_n;
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&bar_acc_empty[acc]));
+        if (++acc == kAccBufs) acc = 0, acc_phase ^= 1u;
+        if (!ok) break;
+        if (own_n > 0) {
+          const int row0 = tc.mb * kBM + quad * 32;
+          const int col0 = tc.nb * kBN + part * kCW + 32 * own_c0;
+          __half* c_line0 = p.c + ((size_t)tc.l * p.m + row0) * (size_t)p.n + col0;
+          const int cols = min(32 * own_n, p.n - col0);
+          if (p.c_lines32)
+            store_lines_coalesced_v8(w, c_line0, p.n, p.m - row0, cols);
+          else
+            store_lines_coalesced(w, c_line0, p.n, p.m - row0, cols);
+        }
+        continue;
+      }
       // SiLU gate -> fp16 words w (this lane's row, 64 columns)
       uint32_t w[32];
       if constexpr (!kSplitK) {
@@ -460,6 +582,9 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
 
   tc_fence_before();
   __syncthreads();
+  // cluster split-K: no CTA exits while a peer may still write into its
+  // shared memory or arrive on its barriers
+  if constexpr (kCluster > 0) cluster_sync();
   if (warp == kEpiWarps + 1) {
     tc_fence_after();
     tmem_dealloc<Cfg::kTmemCols>(tmem);

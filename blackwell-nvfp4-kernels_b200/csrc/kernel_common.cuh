@@ -41,6 +41,22 @@ struct AbortCtl {
       }
     }
   }
+  // Same with cluster-scope acquire (for barriers other CTAs arrive on
+  // after writing into this CTA's shared memory).
+  __device__ __forceinline__ bool wait_cluster(uint32_t bar, uint32_t parity, unsigned bit) const {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    const long long t0 = clock64();
+    while (true) {
+      #pragma unroll 1
+      for (int i = 0; i < 32; ++i)
+        if (mbar_try_wait_cluster(bar, parity)) return true;
+      if (aborted()) return false;
+      if (clock64() - t0 > limit) {
+        raise(bit);
+        return false;
+      }
+    }
+  }
   // Used on the way out after an abort: wait for async work this thread
   // issued (bounded, no new status bits).
   __device__ __forceinline__ void drain(uint32_t bar, uint32_t parity) const {

@@ -20,6 +20,7 @@ enum : unsigned {
   kDevTimeoutAccFree  = 1u << 3,   // MMA issuer waited too long for TMEM
   kDevTimeoutSelftest = 1u << 4,   // the wait self-test ran out (expected)
   kDevTimeoutScales   = 1u << 5,   // MMA issuer waited too long for staged scales
+  kDevTimeoutPeers    = 1u << 6,   // a split-K cluster CTA waited too long for its peers
 };
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
@@ -312,6 +313,25 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(saddr), "r"(rank));
   return r;
+}
+
+// try_wait with cluster-scope acquire: data other CTAs of the cluster wrote
+// before their release-arrive on this barrier is visible once it returns true.
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 P, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, P;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Store to shared memory of any CTA of the cluster (address from mapa).
+__device__ __forceinline__ void st_shared_cluster_f32(uint32_t cluster_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v) : "memory");
 }
 
 // Arrive on an mbarrier that may live in another CTA of the cluster.

@@ -64,14 +64,28 @@ def _validate(a, b1, b2, sfa_perm, sfb1_perm, sfb2_perm, c):
     return m, n, k, l, dev
 
 
+# torch's raw current-device / current-stream queries cost ~0.1 us; the public
+# torch.cuda.current_stream() builds a Stream object (~3 us per call, as much
+# as a small kernel).  The public calls remain the fallback.
+_get_device = getattr(torch._C, "_cuda_getDevice", None)
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
+def _current_stream_handle(index: int) -> int:
+    if _raw_stream is not None:
+        return _raw_stream(index)
+    return torch.cuda.current_stream(index).cuda_stream
+
+
 def on_device(device: torch.device, launch):
     """Run launch(stream_handle) with `device` current (the library launches
     on the current device) and its current stream; the device switch is
     skipped when `device` is current already (the common case)."""
-    if torch.cuda.current_device() == device.index:
-        return launch(torch.cuda.current_stream().cuda_stream)
+    cur = _get_device() if _get_device is not None else torch.cuda.current_device()
+    if cur == device.index:
+        return launch(_current_stream_handle(cur))
     with torch.cuda.device(device):
-        return launch(torch.cuda.current_stream(device).cuda_stream)
+        return launch(_current_stream_handle(device.index))
 
 
 class _Plan:

@@ -12,6 +12,7 @@ from __future__ import annotations
 import torch
 
 from . import _lib
+from .dual_gemm import on_device
 
 
 def quantize(x: torch.Tensor, out=None):
@@ -41,10 +42,8 @@ def quantize(x: torch.Tensor, out=None):
         sf = torch.empty((l, rows, k // 16), dtype=torch.uint8, device=dev)
         sf_perm = torch.empty((l, rb, ka, 32, 4, 4), dtype=torch.uint8, device=dev)
     lib = _lib.load()
-    with torch.cuda.device(dev):
-        stream = torch.cuda.current_stream(dev).cuda_stream
-        _lib.check(lib.nvfp4_quantize(x.data_ptr(), rows, k, l, packed.data_ptr(),
-                                      sf_perm.data_ptr(), sf.data_ptr(), stream))
+    _lib.check(on_device(dev, lambda st: lib.nvfp4_quantize(
+        x.data_ptr(), rows, k, l, packed.data_ptr(), sf_perm.data_ptr(), sf.data_ptr(), st)))
     return (packed.permute(1, 2, 0).view(torch.float4_e2m1fn_x2),
             sf.permute(1, 2, 0).view(torch.float8_e4m3fn),
             sf_perm.permute(3, 4, 1, 5, 2, 0).view(torch.float8_e4m3fn))

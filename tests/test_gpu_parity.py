@@ -110,6 +110,25 @@ def test_dual_split_k(m, n, k, l, splits, monkeypatch):
     assert_close(run_dual(data), oracle_dual(data), f"dual splitK={splits} {m}x{n}x{k}x{l}")
 
 
+@pytest.mark.parametrize("cluster", ["2", "4"])
+@pytest.mark.parametrize("m,n,k,l", [(256, 512, 4096, 1), (200, 264, 2048, 1), (384, 640, 1024, 2),
+                                     (128, 7168, 4096, 1), (256, 3072, 4096, 1), (1, 8, 2048, 1)])
+def test_dual_cluster_split_k(m, n, k, l, cluster, monkeypatch):
+    """Cluster split-K (partials exchanged between the CTAs of a cluster, each
+    CTA reducing and storing its own column slice) at 2 and 4 splits, ragged
+    M/N, batched L; shapes where 4 splits do not fit fall back to 2."""
+    monkeypatch.setenv("NVFP4_DUAL_CLUSTER", cluster)
+    data = I.generate_dual_input(m, n, k, l, seed=int(cluster) * 17 + m, device="cuda")
+    assert_close(run_dual(data), oracle_dual(data), f"dual cluster={cluster} {m}x{n}x{k}x{l}")
+
+
+def test_dual_cluster_split_k_deterministic(monkeypatch):
+    monkeypatch.setenv("NVFP4_DUAL_CLUSTER", "4")
+    data = I.generate_dual_input(256, 1024, 4096, 1, seed=6, device="cuda")
+    outs = [D.custom_kernel(data).clone() for _ in range(3)]
+    assert all(torch.equal(outs[0], o) for o in outs[1:])
+
+
 def test_dual_split_k_deterministic(monkeypatch):
     monkeypatch.setenv("NVFP4_DUAL_SPLITS", "4")
     data = I.generate_dual_input(256, 1024, 4096, 1, seed=5, device="cuda")
