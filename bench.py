@@ -111,6 +111,26 @@ def quant_workload(rank, world, device):
     return xs, 0.0, nbytes, desc
 
 
+def shape_workload(args, device):
+    """--shape M,N,K (dual) or --group-shape M1:M2:..,N,K (grouped): a seeded
+    N(0,1) workload of any size for kernel-only profiling runs."""
+    from nvfp4_b200 import inputs as I
+    g = torch.Generator().manual_seed(11)
+    if args.shape:
+        m, n, k = (int(v) for v in args.shape.split(","))
+        data = I.dual_from_fp32(torch.randn(m, k, generator=g), torch.randn(n, k, generator=g),
+                                torch.randn(n, k, generator=g), device=device)
+        nbytes = m * k // 2 + 2 * n * k // 2 + (m + 2 * n) * k // 16 + 2 * m * n
+        return 1, data, 4.0 * m * n * k, nbytes, dict(workload=f"dual_gemm_{m}x{n}x{k}", m=m, n=n, k=k)
+    ms_s, n_s, k_s = args.group_shape.split(",")
+    ms, n, k = [int(v) for v in ms_s.split(":")], int(n_s), int(k_s)
+    data = I.group_from_fp32([(torch.randn(m, k, generator=g), torch.randn(n, k, generator=g))
+                              for m in ms], device=device)
+    nbytes = sum(m * k // 2 + m * k // 16 + 2 * m * n + n * k // 2 + n * k // 16 for m in ms)
+    return 3, data, sum(2.0 * m * n * k for m in ms), nbytes, \
+        dict(workload=f"grouped_gemm_{'+'.join(map(str, ms))}x{n}x{k}", groups=ms, n=n, k=k)
+
+
 def make_workload(cfg, rank, world, device):
     if cfg == 5:
         return quant_workload(rank, world, device)
@@ -262,6 +282,25 @@ def time_cpu(cfg, data_cpu, budget_s: float, min_reps: int = 1):
     return flops / secs / 1e12, reps, rows, cols
 
 
+def time_cpu_quant(x_dev, budget_s: float):
+    """Oracle quantiser (numpy) on a 1024-row sample of one operand, bytes
+    counted as on the device: fp32 in, e2m1 + plain and permuted scales out."""
+    from oracle import nvfp4_oracle as O
+    x = x_dev[:1024].detach().cpu().numpy()
+    rows, k = x.shape
+    nb = rows * k * 4 + rows * k // 2 + rows * k // 16 * 2
+    O.quantize_nvfp4(x[:16])
+    secs, reps = 0.0, 0
+    while reps < 1 or secs < budget_s:
+        t0 = time.perf_counter()
+        O.quantize_nvfp4(x)
+        secs += time.perf_counter() - t0
+        reps += 1
+    return {"value": round(nb * reps / secs / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"numpy oracle quantiser on {rows}x{k} fp32 rows, {reps} reps "
+                      f"(~{budget_s:.0f} s, single-threaded numpy)"}
+
+
 def cpu_cores():
     try:
         return len(os.sched_getaffinity(0))
@@ -402,7 +441,13 @@ def main():
                     help="device-timed calls only (no e2e, no CPU baseline): the profiling run")
     ap.add_argument("--suite", default=None, choices=["task"],
                     help="task: the reference's own task.yml benchmark shapes, one line per task")
+    ap.add_argument("--shape", default=None,
+                    help="M,N,K: kernel-only dual GEMM at this size (profiling runs)")
+    ap.add_argument("--group-shape", default=None,
+                    help="M1:M2:...,N,K: kernel-only grouped GEMM at these sizes (profiling runs)")
     args = ap.parse_args()
+    if args.shape or args.group_shape:
+        args.kernel_only = True
     assert args.warmup >= 3 or args.impl == "reference", "need >= 3 warm-up steps"
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -425,7 +470,10 @@ def main():
         pg = dist
 
     from nvfp4_b200 import _lib
-    data, flop, nbytes, desc = make_workload(cfg, rank, world, device)
+    if args.shape or args.group_shape:
+        cfg, data, flop, nbytes, desc = shape_workload(args, device)
+    else:
+        data, flop, nbytes, desc = make_workload(cfg, rank, world, device)
     stream = torch.cuda.current_stream(device)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
 
@@ -503,13 +551,18 @@ def main():
     e2e_t = torch.tensor([es.elapsed_time(ee) / 1e3], dtype=torch.float64, device=device)
     if pg:
         pg.all_reduce(e2e_t, op=pg.ReduceOp.MAX)
-    e2e_value = flop_t.item() * args.e2e_steps / e2e_t.item() / 1e12
+    quant = cfg == 5
+    if quant:   # bytes-moved metric for the quantiser
+        e2e_value = bytes_t.item() * args.e2e_steps / e2e_t.item() / 1e9
+    else:
+        e2e_value = flop_t.item() * args.e2e_steps / e2e_t.item() / 1e12
+    unit = "GB/s" if quant else "TFLOP/s"
 
     # ---- roofline of the dominant kernel (the GEMM kernel is the only launch)
     hbm_peak, bf16_peak, peak_kind = load_peaks()
     nvfp4_peak = 4.0 * bf16_peak
     avg_launch_s = statistics.mean(per_call_ms) / 1e3
-    hbm_bound = cfg == 2
+    hbm_bound = cfg in (2, 5)
     traffic = load_traffic(desc["workload"])
     if hbm_bound:
         ach = nbytes / avg_launch_s / 1e9
@@ -525,23 +578,27 @@ def main():
                            if not hbm_bound else f"{peak_kind}: HBM copy {hbm_peak} GB/s")
 
     result = {
-        "metric": metric_name(cfg), "value": round(value, 2), "unit": "TFLOP/s",
+        "metric": metric_name(cfg), "value": round(value, 2), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 5), "us_per_call": round(ms_per_step * 1e3, 2),
         "higher_is_better": True, "scaling": "weak" if cfg in (0, 1, 2) else "strong",
-        "vs_baseline": None, "dtype": "nvfp4(e2m1+e4m3 block16) x nvfp4 -> fp32 acc -> fp16",
+        "vs_baseline": None,
+        "dtype": "fp32 -> e2m1 + e4m3 block16" if quant
+        else "nvfp4(e2m1+e4m3 block16) x nvfp4 -> fp32 acc -> fp16",
         "data": "synthetic: seeded N(0,1) fp32 quantised to NVFP4",
         "config": {**desc, "parallelism": f"{'n-shard' if cfg in (0, 1, 2) else 'expert-lpt'}{world}",
                    "l2": f"flushed ({L2_FLUSH_BYTES >> 20} MiB write) between timed calls"},
-        "e2e": {"value": round(e2e_value, 3), "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+        "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
                 "api": "nvfp4_b200.*.custom_kernel (ctypes -> libnvfp4_b200.so)"},
         "roofline": roof,
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * (len(data) if quant else 1),
         "clocks": clk.summary(),
     }
 
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and quant:
+        result["cpu_baseline"] = time_cpu_quant(data[0][0], args.cpu_budget)
+    elif rank == 0 and world == 1 and not args.no_cpu_baseline:
         dc = cpu_inputs(cfg, data)
         torch.set_num_threads(cpu_cores())
         v, reps, rows, cols = time_cpu(cfg, dc, args.cpu_budget)
