@@ -176,7 +176,7 @@ class ClockSampler:
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
                "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, device_index: int, period_s: float = 0.01):
+    def __init__(self, device_index: int, period_s: float = 0.001):
         self.samples, self.reasons = [], set()
         self.ok = False
         try:

@@ -16,7 +16,7 @@
 
 #include "../../include/nvfp4_b200.h"
 #include "dual_gemm.cuh"
-#include "dual_gemm_pair.cuh"
+#include "dual_gemm_2sm.cuh"
 #include "grouped_gemm.cuh"
 #include "quantize.cuh"
 
@@ -98,7 +98,7 @@ struct Knobs {
   int dual_group_m = 16;   // NVFP4_DUAL_GROUP_M
   int dual_splits = 0;     // NVFP4_DUAL_SPLITS (0 = automatic)
   int dual_bn = 0;         // NVFP4_DUAL_BN (64 / 128; 0 = automatic)
-  bool dual_pair = false;  // NVFP4_DUAL_KERNEL=pair
+  bool dual_pair = false;  // NVFP4_DUAL_KERNEL=pair: the CTA-pair kernel
   int dual_cluster = 0;    // NVFP4_DUAL_CLUSTER: 0 automatic, 1 off, 2 / 4 forced cluster split-K
   int grouped_bn = 0;      // NVFP4_GROUPED_BN (128 / 256; 0 = automatic)
 };
@@ -427,16 +427,20 @@ int launch_dual(DeviceState* d, int slot, DualParams& p, int forced_splits, int 
   return check_launch("dual_gemm_kernel");
 }
 
-template <int kStages>
-int launch_dual_pair(DeviceState* d, int slot, const void* a, const void* b1, const void* b2,
-                     const void* sfa, const void* sfb1, const void* sfb2, void* c, int m, int n,
-                     int k, int l, int group_m, cudaStream_t stream) {
-  using Cfg = DualPairCfg<kStages>;
-  auto kern = dual_gemm_pair_kernel<kStages>;
+// CTA-pair kernel with 96-column tiles, 192-wide MMAs and two accumulator buffers.
+template <int kBN, int kStages>
+int launch_dual_2sm(DeviceState* d, int slot, const void* a, const void* b1, const void* b2,
+                    const void* sfa, const void* sfb1, const void* sfb2, void* c, int m, int n,
+                    int k, int l, int group_m, cudaStream_t stream) {
+  using Cfg = Dual2smCfg<kBN, kStages>;
+  auto kern = dual_gemm_2sm_kernel<kBN, kStages>;
   int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
   if (rc) return rc;
-  DualPairParams p;
+  Dual2smParams p;
   memset(&p, 0, sizeof(p));
+  p.sfa = static_cast<const uint8_t*>(sfa);
+  p.sfb1 = static_cast<const uint8_t*>(sfb1);
+  p.sfb2 = static_cast<const uint8_t*>(sfb2);
   p.c = static_cast<__half*>(c);
   p.m = m, p.n = n, p.k = k, p.l = l;
   p.mp_blocks = (m + 2 * kBM - 1) / (2 * kBM);
@@ -446,17 +450,15 @@ int launch_dual_pair(DeviceState* d, int slot, const void* a, const void* b1, co
   p.sfa_blocks = (m + 127) / 128;
   p.sfb_blocks = (n + 127) / 128;
   p.group_m = group_m;
+  p.c_lines32 = (n % 16 == 0) && (reinterpret_cast<uintptr_t>(c) % 32 == 0);
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
   if ((rc = encode_operand(&p.tmap_a, a, m, k, l, kBM))) return rc;
   if ((rc = encode_operand(&p.tmap_b1, b1, n, k, l, Cfg::kBN))) return rc;
   if ((rc = encode_operand(&p.tmap_b2, b2, n, k, l, Cfg::kBN))) return rc;
-  if ((rc = encode_scales(&p.tmap_sfa, sfa, l * p.sfa_blocks, k))) return rc;
-  if ((rc = encode_scales(&p.tmap_sfb1, sfb1, l * p.sfb_blocks, k))) return rc;
-  if ((rc = encode_scales(&p.tmap_sfb2, sfb2, l * p.sfb_blocks, k))) return rc;
   const int pairs = p.tiles < d->num_sms / 2 ? p.tiles : d->num_sms / 2;
   kern<<<2 * pairs, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
-  return check_launch("dual_gemm_pair_kernel");
+  return check_launch("dual_gemm_2sm_kernel");
 }
 
 // ---------------------------------------------------------------- grouped GEMM
@@ -543,14 +545,20 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
 
-  // Kernel choice: single-CTA 128-wide tiles, or 64-wide tiles when those
-  // would leave SMs idle.  The CTA-pair kernel (NVFP4_DUAL_KERNEL=pair) loads
-  // 30% fewer operand bytes per SM but measures slower on B200: its
-  // tcgen05.cp.cta_group::2 scale copies run ~2x longer than the single-CTA
-  // copies and serialise with the MMAs in the tensor pipe.
-  if (kn.dual_pair)
-    return launch_dual_pair<5>(d, 2, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l, kn.dual_group_m,
-                               stream);
+  // Kernel choice: the single-CTA kernel (128-wide tiles; cluster split-K
+  // when the tiles leave SMs idle; 64-wide tiles on request).  The CTA-pair
+  // kernel (NVFP4_DUAL_KERNEL=pair; 96-wide tiles with NVFP4_DUAL_BN=96)
+  // loads a third fewer operand bytes per SM and issues half the MMA
+  // instructions, but measures ~8% slower on configuration 1 (478 vs 443 us;
+  // 96-wide: 618 us): the pair's two-CTA handshakes on every stage cost more
+  // than the bytes save.
+  if (kn.dual_pair) {
+    if (kn.dual_bn == 96)
+      return launch_dual_2sm<96, 5>(d, 3, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
+                                    kn.dual_group_m, stream);
+    return launch_dual_2sm<128, 5>(d, 14, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
+                                   kn.dual_group_m, stream);
+  }
   // 128-wide tiles (one fused N=256 MMA per K step), split along K when
   // there are fewer tiles than SMs; 64-wide tiles only on request.
   int bn = 128;

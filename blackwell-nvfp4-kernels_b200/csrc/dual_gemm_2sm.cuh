@@ -1,0 +1,379 @@
+// NVFP4 dual GEMM on CTA pairs with 192-wide MMAs and double-buffered
+// accumulators, sm_100a: the large-problem kernel.
+//
+//   C = silu(A . B1ᵀ) * (A . B2ᵀ)   (fp32 accumulate in TMEM, fp16 out)
+//
+// Same computation as the reference's ref_kernel
+// (nvfp4_dual_gemm/reference.py:27-77); own design:
+//
+// * a CTA pair (cluster of 2 on neighbouring SMs) owns a 256 x 96 tile of C.
+//   CTA r holds A rows [256*mp + 128*r, +128) and one 96-row B tile: CTA 0
+//   the B1 rows of the tile's columns, CTA 1 the B2 rows.  One
+//   tcgen05.mma.cta_group::2 with M = 256, N = 192 per 64-deep K step then
+//   writes, in each CTA's TMEM, its 128 rows x [gate 96 | up 96].  Per SM
+//   and K step: A 16 KB + B 12 KB of operands for 128 x 192 outputs (the
+//   single-CTA kernel: 48 KB for 128 x 256), and one MMA instruction covers
+//   both SMs;
+// * one 192-column accumulator; eight epilogue warps pull all of it into
+//   registers (48 gate + 48 up columns per warp) and release it before the
+//   math and the stores, so the next tile's MMAs start early;
+// * scale factors: each CTA bulk-loads its A atoms and the atom blocks that
+//   cover the tile's 96 B1 and 96 B2 rows (a 96-row tile need not start on a
+//   128-row atom) onto a landing barrier; four staging warps per CTA gather
+//   row i of every needed atom column into TMEM lane i of each quadrant with
+//   tcgen05.st (SFA: 4 columns per K step; SFB: columns c = 0..5 hold B rows
+//   32c..32c+31 of the 192-row MMA operand) and arrive on the leader's
+//   per-stage barrier.  Each pipeline stage owns one TMEM scale buffer (48
+//   columns): refilling a stage already waits for the MMAs that read it.
+//   (Two accumulator buffers would leave room for only two scale buffers,
+//   which put the commit -> staging -> MMA chain on every K block's critical
+//   path: 2.6x slower, measured.);
+// * both producers count their tile bytes on the leader's stage barrier
+//   (TMA .cta_group::2, no multicast); the leader commits to both CTAs
+//   (tcgen05.commit multicast); epilogue warps of both CTAs release an
+//   accumulator buffer with arrivals on the leader's barrier; cluster
+//   barriers bracket setup and teardown.  All waits are bounded.
+#pragma once
+#include <cuda.h>
+#include "kernel_common.cuh"
+
+namespace nvfp4 {
+
+struct Dual2smParams {
+  CUtensorMap tmap_a;    // bytes [L][M][K/2], box {128 B, 128 rows, 1}
+  CUtensorMap tmap_b1;   // bytes [L][N][K/2], box {128 B, 96 rows, 1}
+  CUtensorMap tmap_b2;
+  const uint8_t* sfa;    // permuted scale atoms [L][ceil(M/128)][K/64][512]
+  const uint8_t* sfb1;   // [L][ceil(N/128)][K/64][512]
+  const uint8_t* sfb2;
+  __half* c;             // [L][M][N]
+  int m, n, k, l;
+  int mp_blocks, n_blocks, k_blocks, tiles;  // 256-row pair blocks, 96-column blocks
+  int sfa_blocks, sfb_blocks;                // ceil(M/128), ceil(N/128)
+  int group_m;                               // raster: pair M-blocks per group
+  int c_lines32;                             // C rows start 32-byte aligned
+  unsigned* status;
+  long long wait_limit;
+};
+
+template <int kBN_, int kStages>
+struct Dual2smCfg {
+  static constexpr int kBN = kBN_;                     // C columns per tile: 96 or 128
+  static constexpr int kNmma = 2 * kBN;                // pair MMA N = [B1 tile ; B2 tile]
+  static constexpr int kGroups = kBN / 32;             // 32-row groups per B tile
+  static constexpr int kSfbBlocks = kBN == 128 ? 1 : 2;   // 128-row atom blocks covering a tile
+  static constexpr int kABytes = kBM * kBK / 2;        // 16 KB
+  static constexpr int kBBytes = kBN * kBK / 2;        // 12 or 16 KB
+  static constexpr int kSfaBytes = kSfStageBytes;      // 4 atoms of this CTA's A rows
+  static constexpr int kSfbBytes = kSfbBlocks * kSfStageBytes;   // per B operand
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + 2 * kSfbBytes;   // 38 KB
+  static constexpr int kPairTxBytes = 2 * (kABytes + kBBytes);
+  static constexpr int kEpiWarps = 8;                   // 2 per TMEM quadrant
+  static constexpr int kColsPerWarp = kBN / 2;         // 48 or 64 columns of gate and of up
+  static constexpr int kSfWarps = 4;
+  static constexpr int kProdWarp = kEpiWarps, kMmaWarp = kEpiWarps + 1;
+  static constexpr int kThreads = 32 * (kEpiWarps + 2 + kSfWarps);
+  static constexpr int kSmemBytes = kStages * kStageBytes + 1024;
+  static constexpr int kTmemCols = 512;
+  static constexpr int kAccBufs = 1;
+  static constexpr int kAccCols = kNmma;
+  static constexpr int kSfCol = kAccBufs * kAccCols;   // 192
+  static constexpr int kSfBufCols = 48;                // per stage: SFA 4x4 + SFB 4x8 (6 used)
+  static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned");
+  static_assert(kSfCol + kStages * kSfBufCols <= kTmemCols, "TMEM budget: one scale buffer per stage");
+  static_assert(kBN == 96 || kBN == 128, "tile width");
+};
+
+struct PairTile2 { int l, mp, nb; };
+
+__device__ __forceinline__ PairTile2 pair2_tile_coord(const Dual2smParams& p, int t) {
+  const int per_l = p.mp_blocks * p.n_blocks;
+  PairTile2 tc;
+  tc.l = t / per_l;
+  const int local = t - tc.l * per_l;
+  const int span = p.group_m * p.n_blocks;
+  const int g = local / span;
+  const int first = g * p.group_m;
+  const int gsz = min(p.mp_blocks - first, p.group_m);
+  const int r = local - g * span;
+  tc.mp = first + r % gsz;
+  tc.nb = r / gsz;
+  return tc;
+}
+
+template <int kBN, int kStages>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Dual2smCfg<kBN, kStages>::kThreads, 1)
+dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
+  using Cfg = Dual2smCfg<kBN, kStages>;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ uint64_t bar_full[kStages], bar_empty[kStages];
+  __shared__ uint64_t bar_sf_landed[kStages], bar_sf_full[kStages];
+  __shared__ uint64_t bar_acc_full[Cfg::kAccBufs], bar_acc_empty[Cfg::kAccBufs];
+  __shared__ uint64_t bar_drain;
+  __shared__ uint32_t s_tmem_base;
+  __shared__ volatile int s_abort;
+
+  const uint32_t smem_base = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const int warp = threadIdx.x >> 5;
+  const uint32_t lane = lane_id();
+  const uint32_t rank = cluster_ctarank();   // 0 = leader
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, num_pairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&bar_full[s]), 1);
+      mbar_init(smem_u32(&bar_empty[s]), 1);
+      mbar_init(smem_u32(&bar_sf_landed[s]), 1);
+      mbar_init(smem_u32(&bar_sf_full[s]), 2 * Cfg::kSfWarps);      // both CTAs' staging warps
+    }
+    for (int b = 0; b < Cfg::kAccBufs; ++b) {
+      mbar_init(smem_u32(&bar_acc_full[b]), 1);
+      mbar_init(smem_u32(&bar_acc_empty[b]), 2 * Cfg::kEpiWarps);   // both CTAs' epilogue warps
+    }
+    mbar_init(smem_u32(&bar_drain), 1);
+    s_abort = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == Cfg::kProdWarp && lane == 0) {
+    tma_prefetch_desc(&p.tmap_a);
+    tma_prefetch_desc(rank == 0 ? &p.tmap_b1 : &p.tmap_b2);
+  }
+  if (warp == Cfg::kMmaWarp) tmem_alloc_pair<Cfg::kTmemCols>(smem_u32(&s_tmem_base));
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();   // the peer's barriers exist before anyone signals them
+  tc_fence_after();
+  const uint32_t tmem = s_tmem_base;
+  const AbortCtl ctl{&s_abort, p.status, p.wait_limit};
+  const int rest_k = p.k / kKStep;   // 64-deep atoms per 128-row block
+
+  if (warp == Cfg::kProdWarp) {
+    // ------------------------------------------------------------ TMA producer (both CTAs)
+    if (lane == 0) {
+      const uint64_t pol = policy_evict_normal();
+      const CUtensorMap* tmap_b = rank == 0 ? &p.tmap_b1 : &p.tmap_b2;
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t last_phase[kStages];
+      bool issued[kStages];
+      for (int s = 0; s < kStages; ++s) issued[s] = false, last_phase[s] = 0;
+      bool ok = true;
+      for (int t = pair; t < p.tiles && ok; t += num_pairs) {
+        const PairTile2 tc = pair2_tile_coord(p, t);
+        const int m0 = tc.mp * 2 * kBM + (int)rank * kBM;   // this CTA's A rows
+        const int n0 = tc.nb * Cfg::kBN;
+        const int blk0 = n0 / 128;
+        const int blk1 = min(blk0 + 1, p.sfb_blocks - 1);   // past N: re-read the last block
+        const size_t atoms = (size_t)rest_k * kSfAtom;
+        const uint8_t* sfa_t = p.sfa + ((size_t)tc.l * p.sfa_blocks + m0 / 128) * atoms;
+        const uint8_t* sfb1_0 = p.sfb1 + ((size_t)tc.l * p.sfb_blocks + blk0) * atoms;
+        const uint8_t* sfb1_1 = p.sfb1 + ((size_t)tc.l * p.sfb_blocks + blk1) * atoms;
+        const uint8_t* sfb2_0 = p.sfb2 + ((size_t)tc.l * p.sfb_blocks + blk0) * atoms;
+        const uint8_t* sfb2_1 = p.sfb2 + ((size_t)tc.l * p.sfb_blocks + blk1) * atoms;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!ctl.wait(smem_u32(&bar_empty[stage]), phase ^ 1u, kDevTimeoutStageFree)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
+          const uint32_t sb = sa + Cfg::kABytes;
+          const uint32_t ssf = sb + Cfg::kBBytes;
+          // scales first, on this CTA's own landing barrier
+          const uint32_t landed = smem_u32(&bar_sf_landed[stage]);
+          mbar_arrive_expect_tx(landed, Cfg::kSfaBytes + 2 * Cfg::kSfbBytes);
+          const size_t so = (size_t)kb * kSfStageBytes;
+          // [SFA][SFB1 block 0 (, 1)][SFB2 block 0 (, 1)]
+          const uint32_t sb1 = ssf + Cfg::kSfaBytes, sb2 = sb1 + Cfg::kSfbBytes;
+          bulk_load(ssf, sfa_t + so, kSfStageBytes, landed, pol);
+          bulk_load(sb1, sfb1_0 + so, kSfStageBytes, landed, pol);
+          bulk_load(sb2, sfb2_0 + so, kSfStageBytes, landed, pol);
+          if constexpr (Cfg::kSfbBlocks == 2) {
+            bulk_load(sb1 + kSfStageBytes, sfb1_1 + so, kSfStageBytes, landed, pol);
+            bulk_load(sb2 + kSfStageBytes, sfb2_1 + so, kSfStageBytes, landed, pol);
+          }
+          // operand tiles: both CTAs' bytes complete on the leader's stage barrier
+          const uint32_t full = mapa_shared(smem_u32(&bar_full[stage]), 0);
+          if (leader) mbar_arrive_expect_tx(smem_u32(&bar_full[stage]), Cfg::kPairTxBytes);
+          tma_load_3d_pair(sa, &p.tmap_a, full, kb * 128, m0, tc.l, pol);
+          tma_load_3d_pair(sb, tmap_b, full, kb * 128, n0, tc.l, pol);
+          issued[stage] = true;
+          last_phase[stage] = phase;
+          if (++stage == kStages) stage = 0, phase ^= 1u;
+        }
+      }
+      if (!ok) {  // in-flight copies land before the CTA winds down
+        for (int s = 0; s < kStages; ++s)
+          if (issued[s]) {
+            ctl.drain(smem_u32(&bar_sf_landed[s]), last_phase[s]);
+            if (leader) ctl.drain(smem_u32(&bar_full[s]), last_phase[s]);
+          }
+      }
+    }
+  } else if (warp == Cfg::kMmaWarp) {
+    // ------------------------------------------------------------ MMA issuer (leader only)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = (1u << 7) | (1u << 10) | ((uint32_t)(Cfg::kNmma >> 3) << 17) |
+                                 ((uint32_t)(256 >> 4) << 24);   // M=256, N=192, e2m1 x e2m1, e4m3 scales
+      constexpr uint16_t kBoth = 0x3;
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true, any = false;
+      for (int t = pair; t < p.tiles && ok; t += num_pairs) {
+        if (!ctl.wait(smem_u32(&bar_acc_empty[acc]), acc_phase ^ 1u, kDevTimeoutAccFree)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_acc = tmem + acc * Cfg::kAccCols;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!ctl.wait(smem_u32(&bar_full[stage]), phase, kDevTimeoutTmaFull) ||
+              !ctl.wait(smem_u32(&bar_sf_full[stage]), phase, kDevTimeoutScales)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
+          const uint32_t sb = sa + Cfg::kABytes;
+          const uint32_t sf_a = tmem + Cfg::kSfCol + stage * Cfg::kSfBufCols;
+          const uint32_t sf_b = sf_a + 16;
+          #pragma unroll
+          for (int j = 0; j < kBK / kKStep; ++j)
+            tc_mma_nvf4_pair(d_acc, kmajor_sw128_desc(sa + 32 * j), kmajor_sw128_desc(sb + 32 * j),
+                             idesc, sf_a + 4 * j, sf_b + 8 * j, (kb | j) != 0);
+          tc_commit_pair(smem_u32(&bar_empty[stage]), kBoth);   // stage (and scale buffer) free
+          any = true;
+          if (++stage == kStages) stage = 0, phase ^= 1u;
+        }
+        if (!ok) break;
+        tc_commit_pair(smem_u32(&bar_acc_full[acc]), kBoth);
+        if (++acc == Cfg::kAccBufs) acc = 0, acc_phase ^= 1u;
+      }
+      if (!ok && any) {
+        tc_commit_pair(smem_u32(&bar_drain), 0x1);
+        ctl.drain(smem_u32(&bar_drain), 0);
+      }
+    }
+  } else if (warp >= Cfg::kEpiWarps + 2) {
+    // ------------------------------------------------------------ scale staging (both CTAs)
+    // Warp w writes TMEM lanes [32*(w%4), +32) of its own CTA.  Lane i of every
+    // quadrant receives row i of each atom column the MMA reads: SFA atom j in
+    // columns [4j, +4) (this CTA's 128 A rows); SFB column 8j + c, c = 0..5,
+    // the scales of B rows 32c + i of the 192-row operand (c < 3: B1 tile rows,
+    // c >= 3: B2 tile rows), gathered from the 128-row atom blocks.
+    const uint32_t t_quad = ((uint32_t)(warp & 3) * 32u) << 16;
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int t = pair; t < p.tiles && ok; t += num_pairs) {
+      const PairTile2 tc = pair2_tile_coord(p, t);
+      const int n0 = tc.nb * Cfg::kBN;
+      const int blk0 = n0 / 128;
+      // for row group c' of a B tile: which loaded atom block, and which
+      // 4-byte column of the atom row
+      uint32_t off[Cfg::kGroups];
+      #pragma unroll
+      for (int c = 0; c < Cfg::kGroups; ++c) {
+        const int r = n0 + 32 * c;
+        off[c] = (uint32_t)((r / 128 - blk0) * kSfStageBytes + ((r / 32) & 3) * 4);
+      }
+      for (int kb = 0; kb < p.k_blocks; ++kb) {
+        // the stage's scales landed (its refill already waited for the MMAs
+        // that read this stage's scale buffer)
+        bool got = true;
+        if (lane == 0) got = ctl.wait(smem_u32(&bar_sf_landed[stage]), phase, kDevTimeoutTmaFull);
+        if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) {
+          ok = false;
+          break;
+        }
+        mbar_try_wait(smem_u32(&bar_sf_landed[stage]), phase);   // every lane observes the phase
+        tc_fence_after();
+        const uint32_t ssf = smem_base + stage * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes;
+        const uint32_t row = lane * 16u;
+        uint32_t ra[16], rb[32];
+        #pragma unroll
+        for (int j = 0; j < kBK / kKStep; ++j) {
+          const uint4 a = lds_v4(ssf + j * kSfAtom + row);
+          ra[4 * j + 0] = a.x, ra[4 * j + 1] = a.y, ra[4 * j + 2] = a.z, ra[4 * j + 3] = a.w;
+          #pragma unroll
+          for (int c = 0; c < 2 * Cfg::kGroups; ++c) {
+            const int op = c / Cfg::kGroups;   // 0: B1 rows, 1: B2 rows
+            const uint32_t base = ssf + Cfg::kSfaBytes + op * Cfg::kSfbBytes;
+            rb[8 * j + c] = lds_u32(base + off[c % Cfg::kGroups] + j * kSfAtom + row);
+          }
+          #pragma unroll
+          for (int c = 2 * Cfg::kGroups; c < 8; ++c) rb[8 * j + c] = 0u;
+        }
+        const uint32_t t_buf = tmem + t_quad + Cfg::kSfCol + stage * Cfg::kSfBufCols;
+        tmem_st_32x32b_x16(t_buf, ra);
+        tmem_st_32x32b_x32(t_buf + 16, rb);
+        tmem_st_wait();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&bar_sf_full[stage]), 0));
+        if (++stage == kStages) stage = 0, phase ^= 1u;
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;        // TMEM lane quadrant
+    const int part = warp >> 2;       // columns [kColsPerWarp*part, +kColsPerWarp) of gate and up
+    constexpr int kCW = Cfg::kColsPerWarp;
+    constexpr int kC16 = kCW / 16;
+    const uint32_t acc_empty_leader = mapa_shared(smem_u32(&bar_acc_empty[0]), 0);
+    uint32_t acc_phase = 0;
+    for (int t = pair; t < p.tiles; t += num_pairs) {
+      const PairTile2 tc = pair2_tile_coord(p, t);
+      if (!ctl.wait(smem_u32(&bar_acc_full[0]), acc_phase, kDevTimeoutAccFull)) break;
+      tc_fence_after();
+      const uint32_t t_gate = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(kCW * part);
+      const uint32_t t_up = t_gate + Cfg::kBN;
+      // pull this warp's gate and up columns into registers, hand TMEM back
+      uint32_t g[kC16][16], u[kC16][16];
+      #pragma unroll
+      for (int c = 0; c < kC16; ++c) {
+        tmem_ld_32x32b_x16(t_gate + 16 * c, g[c]);
+        tmem_ld_32x32b_x16(t_up + 16 * c, u[c]);
+      }
+      tmem_ld_wait();
+      #pragma unroll
+      for (int c = 0; c < kC16; ++c) tmem_regs_ready16(g[c]), tmem_regs_ready16(u[c]);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote(acc_empty_leader);
+      acc_phase ^= 1u;
+      uint32_t w[32];
+      #pragma unroll
+      for (int c = 0; c < kC16; ++c)
+        #pragma unroll
+        for (int e = 0; e < 8; ++e)
+          w[8 * c + e] = pack_half2(silu_gate(__uint_as_float(g[c][2 * e]), __uint_as_float(u[c][2 * e])),
+                                    silu_gate(__uint_as_float(g[c][2 * e + 1]),
+                                              __uint_as_float(u[c][2 * e + 1])));
+      #pragma unroll
+      for (int e = 8 * kC16; e < 32; ++e) w[e] = 0u;
+      // kCW columns per row (48: three 32-byte chunks of a line, 64: a line)
+      const int row0 = tc.mp * 2 * kBM + (int)rank * kBM + quad * 32;
+      const int col0 = tc.nb * Cfg::kBN + kCW * part;
+      __half* c_line0 = p.c + ((size_t)tc.l * p.m + row0) * (size_t)p.n + col0;
+      const int cols = min(kCW, p.n - col0);
+      if (p.c_lines32)
+        store_lines_coalesced_v8(w, c_line0, p.n, p.m - row0, cols);
+      else
+        store_lines_coalesced(w, c_line0, p.n, p.m - row0, cols);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();   // no MMA, copy or remote arrive of either CTA is still in flight
+  if (warp == Cfg::kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc_pair<Cfg::kTmemCols>(tmem);
+  }
+}
+
+}  // namespace nvfp4

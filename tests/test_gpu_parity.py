@@ -72,23 +72,39 @@ def run_dual(data):
     return out.cpu().numpy()
 
 
-@pytest.mark.parametrize("kernel", ["auto", "pair"])
+@pytest.mark.parametrize("kernel", ["auto", "pair", "pair96"])
 @pytest.mark.parametrize("m,n,k,l", DUAL_TASK_TESTS)
 def test_dual_task_shapes(m, n, k, l, kernel, monkeypatch):
     if kernel != "auto":
-        monkeypatch.setenv("NVFP4_DUAL_KERNEL", kernel)
+        monkeypatch.setenv("NVFP4_DUAL_KERNEL", "pair")
+    if kernel == "pair96":
+        monkeypatch.setenv("NVFP4_DUAL_BN", "96")
     data = I.generate_dual_input(m, n, k, l, seed=1111, device="cuda")
     assert_close(run_dual(data), oracle_dual(data), f"dual {kernel} {m}x{n}x{k}")
 
 
 @pytest.mark.parametrize("m,n,k,l", [(256, 128, 256, 1), (384, 640, 1024, 2), (200, 264, 512, 1),
                                      (130, 72, 768, 1), (1, 8, 256, 1), (1000, 1000, 2048, 1)])
-def test_dual_pair_kernel_edges(m, n, k, l, monkeypatch):
-    """CTA-pair kernel: M not a multiple of 256 (second CTA partly or wholly
-    past M), N not a multiple of 128, batched L."""
+@pytest.mark.parametrize("bn", ["128", "96"])
+def test_dual_pair_kernel_edges(m, n, k, l, bn, monkeypatch):
+    """CTA-pair kernel (128- and 96-wide tiles): M not a multiple of 256
+    (second CTA partly or wholly past M), N not a multiple of the tile width,
+    batched L."""
     monkeypatch.setenv("NVFP4_DUAL_KERNEL", "pair")
+    monkeypatch.setenv("NVFP4_DUAL_BN", bn)
+    kernel = f"pair{bn}"
     data = I.generate_dual_input(m, n, k, l, seed=7 + m + n, device="cuda")
-    assert_close(run_dual(data), oracle_dual(data), f"dual pair {m}x{n}x{k}x{l}")
+    assert_close(run_dual(data), oracle_dual(data), f"dual {kernel} {m}x{n}x{k}x{l}")
+
+
+@pytest.mark.parametrize("m,n,k", [(512, 960, 1024), (300, 200, 2048), (256, 96, 256), (768, 2304, 512)])
+def test_dual_pair96_tile_edges(m, n, k, monkeypatch):
+    """CTA-pair kernel with 96-column tiles: scale rows gathered across two
+    128-row atoms, the last tile partly past N, several tiles per pair."""
+    monkeypatch.setenv("NVFP4_DUAL_KERNEL", "pair")
+    monkeypatch.setenv("NVFP4_DUAL_BN", "96")
+    data = I.generate_dual_input(m, n, k, 1, seed=11 + m + n, device="cuda")
+    assert_close(run_dual(data), oracle_dual(data), f"dual pair96 {m}x{n}x{k}")
 
 
 @pytest.mark.parametrize("bn", ["64", "128"])
