@@ -95,9 +95,9 @@ int env_int(const char* name, int dflt) {
 // ~1 us of host time per call matters for microsecond-scale problems.  They
 // are re-read on every call so a process can change them between calls.
 struct Knobs {
-  int dual_group_m = 16;   // NVFP4_DUAL_GROUP_M
+  int dual_group_m = 32;   // NVFP4_DUAL_GROUP_M (measured: 16 -> 32 saves ~1.5% on 8192x14336x4096)
   int dual_splits = 0;     // NVFP4_DUAL_SPLITS (0 = automatic)
-  int dual_bn = 0;         // NVFP4_DUAL_BN (64 / 128; 0 = automatic)
+  int dual_bn = 0;         // NVFP4_DUAL_BN (64 / 128, or 96 / 128 for the pair kernel; 0 = automatic)
   bool dual_pair = false;  // NVFP4_DUAL_KERNEL=pair: the CTA-pair kernel
   int dual_cluster = 0;    // NVFP4_DUAL_CLUSTER: 0 automatic, 1 off, 2 / 4 forced cluster split-K
   int grouped_bn = 0;      // NVFP4_GROUPED_BN (128 / 256; 0 = automatic)
@@ -762,7 +762,7 @@ extern "C" int nvfp4_dual_gemm_noalloc(const void* a, const void* b1, const void
   p.n_blocks = (n + kBN - 1) / kBN;
   p.k_blocks = k / kBK;
   p.tiles = l * p.m_blocks * p.n_blocks;
-  p.group_m = env_int("NVFP4_DUAL_GROUP_M", 16);
+  p.group_m = env_int("NVFP4_DUAL_GROUP_M", 32);
   if (p.group_m < 1) p.group_m = 1;
   p.splits = choose_splits(p.tiles, p.k_blocks, d->num_sms);
   const int forced = env_int("NVFP4_DUAL_SPLITS", 0);
