@@ -182,24 +182,6 @@ int encode_operand_uncached(CUtensorMap* map, const void* base, int rows, int k,
   return NVFP4_OK;
 }
 
-// Permuted scale tensor viewed as u64 [blocks][K/64][64] (one 512-byte atom =
-// 64 u64), box {64, 4, 1} = the four atoms of one 256-deep K step.  `blocks`
-// counts 128-row blocks over all batches (L * ceil(rows/128)).
-int encode_scales_uncached(CUtensorMap* map, const void* base, int blocks, int k) {
-  const cuuint64_t dims[3] = {64u, (cuuint64_t)(k / 64), (cuuint64_t)blocks};
-  const cuuint64_t strides[2] = {512u, (cuuint64_t)(k / 64) * 512u};
-  const cuuint32_t box[3] = {64u, 4u, 1u};
-  const cuuint32_t estr[3] = {1u, 1u, 1u};
-  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT64, 3, const_cast<void*>(base), dims,
-                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  if (r != CUDA_SUCCESS)
-    return fail(NVFP4_ERR_CUDA, "cuTensorMapEncodeTiled (scales) failed (%d) blocks=%d k=%d",
-                (int)r, blocks, k);
-  return NVFP4_OK;
-}
-
 // Encoded descriptors are pure functions of (address, rows, K, L, box rows);
 // repeated calls on the same tensors (the common case: weights, persistent
 // activation buffers) reuse them instead of re-encoding.
@@ -238,12 +220,6 @@ int cached_map(CUtensorMap* map, const MapKey& key, Encode encode) {
   if (g_maps.size() >= kMaxCachedMaps) g_maps.clear();
   g_maps.emplace(key, *map);
   return NVFP4_OK;
-}
-
-int encode_scales(CUtensorMap* map, const void* base, int blocks, int k) {
-  // box == -1 marks the scale-tensor view in the shared cache
-  const MapKey key{reinterpret_cast<uintptr_t>(base), blocks, k, 1, -1};
-  return cached_map(map, key, [&] { return encode_scales_uncached(map, base, blocks, k); });
 }
 
 int encode_operand(CUtensorMap* map, const void* base, int rows, int k, int l, int box_rows) {

@@ -261,9 +261,10 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
     // ------------------------------------------------------------ scale staging (both CTAs)
     // Warp w writes TMEM lanes [32*(w%4), +32) of its own CTA.  Lane i of every
     // quadrant receives row i of each atom column the MMA reads: SFA atom j in
-    // columns [4j, +4) (this CTA's 128 A rows); SFB column 8j + c, c = 0..5,
-    // the scales of B rows 32c + i of the 192-row operand (c < 3: B1 tile rows,
-    // c >= 3: B2 tile rows), gathered from the 128-row atom blocks.
+    // columns [4j, +4) (this CTA's 128 A rows); SFB column 8j + c,
+    // c < 2 * kGroups, the scales of B rows 32c + i of the 2*kBN-row operand
+    // (c < kGroups: B1 tile rows, then B2 tile rows), gathered from the
+    // 128-row atom blocks (128-wide tiles: whole atom rows).
     const uint32_t t_quad = ((uint32_t)(warp & 3) * 32u) << 16;
     int stage = 0;
     uint32_t phase = 0;
@@ -298,14 +299,22 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
         for (int j = 0; j < kBK / kKStep; ++j) {
           const uint4 a = lds_v4(ssf + j * kSfAtom + row);
           ra[4 * j + 0] = a.x, ra[4 * j + 1] = a.y, ra[4 * j + 2] = a.z, ra[4 * j + 3] = a.w;
-          #pragma unroll
-          for (int c = 0; c < 2 * Cfg::kGroups; ++c) {
-            const int op = c / Cfg::kGroups;   // 0: B1 rows, 1: B2 rows
-            const uint32_t base = ssf + Cfg::kSfaBytes + op * Cfg::kSfbBytes;
-            rb[8 * j + c] = lds_u32(base + off[c % Cfg::kGroups] + j * kSfAtom + row);
+          if constexpr (Cfg::kBN == 128) {
+            // the tile is one whole atom block of B1 and of B2: atom rows as they are
+            const uint4 b1 = lds_v4(ssf + Cfg::kSfaBytes + j * kSfAtom + row);
+            const uint4 b2 = lds_v4(ssf + Cfg::kSfaBytes + Cfg::kSfbBytes + j * kSfAtom + row);
+            rb[8 * j + 0] = b1.x, rb[8 * j + 1] = b1.y, rb[8 * j + 2] = b1.z, rb[8 * j + 3] = b1.w;
+            rb[8 * j + 4] = b2.x, rb[8 * j + 5] = b2.y, rb[8 * j + 6] = b2.z, rb[8 * j + 7] = b2.w;
+          } else {
+            #pragma unroll
+            for (int c = 0; c < 2 * Cfg::kGroups; ++c) {
+              const int op = c / Cfg::kGroups;   // 0: B1 rows, 1: B2 rows
+              const uint32_t base = ssf + Cfg::kSfaBytes + op * Cfg::kSfbBytes;
+              rb[8 * j + c] = lds_u32(base + off[c % Cfg::kGroups] + j * kSfAtom + row);
+            }
+            #pragma unroll
+            for (int c = 2 * Cfg::kGroups; c < 8; ++c) rb[8 * j + c] = 0u;
           }
-          #pragma unroll
-          for (int c = 2 * Cfg::kGroups; c < 8; ++c) rb[8 * j + c] = 0u;
         }
         const uint32_t t_buf = tmem + t_quad + Cfg::kSfCol + stage * Cfg::kSfBufCols;
         tmem_st_32x32b_x16(t_buf, ra);
