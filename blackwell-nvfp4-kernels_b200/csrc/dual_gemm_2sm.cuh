@@ -156,9 +156,8 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
       const CUtensorMap* tmap_b = rank == 0 ? &p.tmap_b1 : &p.tmap_b2;
       int stage = 0;
       uint32_t phase = 0;
-      uint32_t last_phase[kStages];
-      bool issued[kStages];
-      for (int s = 0; s < kStages; ++s) issued[s] = false, last_phase[s] = 0;
+      // per stage: ever issued, and the phase of its last issue (abort drain)
+      uint32_t issued = 0, last_phase = 0;
       bool ok = true;
       for (int t = pair; t < p.tiles && ok; t += num_pairs) {
         const PairTile2 tc = pair2_tile_coord(p, t);
@@ -198,16 +197,16 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
           if (leader) mbar_arrive_expect_tx(smem_u32(&bar_full[stage]), Cfg::kPairTxBytes);
           tma_load_3d_pair(sa, &p.tmap_a, full, kb * 128, m0, tc.l, pol);
           tma_load_3d_pair(sb, tmap_b, full, kb * 128, n0, tc.l, pol);
-          issued[stage] = true;
-          last_phase[stage] = phase;
+          issued |= 1u << stage;
+          last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == kStages) stage = 0, phase ^= 1u;
         }
       }
       if (!ok) {  // in-flight copies land before the CTA winds down
         for (int s = 0; s < kStages; ++s)
-          if (issued[s]) {
-            ctl.drain(smem_u32(&bar_sf_landed[s]), last_phase[s]);
-            if (leader) ctl.drain(smem_u32(&bar_full[s]), last_phase[s]);
+          if ((issued >> s) & 1u) {
+            ctl.drain(smem_u32(&bar_sf_landed[s]), (last_phase >> s) & 1u);
+            if (leader) ctl.drain(smem_u32(&bar_full[s]), (last_phase >> s) & 1u);
           }
       }
     }
@@ -341,29 +340,51 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
       const uint32_t t_gate = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(kCW * part);
       const uint32_t t_up = t_gate + Cfg::kBN;
       // pull this warp's gate and up columns into registers, hand TMEM back
-      uint32_t g[kC16][16], u[kC16][16];
-      #pragma unroll
-      for (int c = 0; c < kC16; ++c) {
-        tmem_ld_32x32b_x16(t_gate + 16 * c, g[c]);
-        tmem_ld_32x32b_x16(t_up + 16 * c, u[c]);
-      }
-      tmem_ld_wait();
-      #pragma unroll
-      for (int c = 0; c < kC16; ++c) tmem_regs_ready16(g[c]), tmem_regs_ready16(u[c]);
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_remote(acc_empty_leader);
-      acc_phase ^= 1u;
       uint32_t w[32];
-      #pragma unroll
-      for (int c = 0; c < kC16; ++c)
+      if constexpr (kCW == 64) {
+        uint32_t g[2][32], u[2][32];
         #pragma unroll
-        for (int e = 0; e < 8; ++e)
-          w[8 * c + e] = pack_half2(silu_gate(__uint_as_float(g[c][2 * e]), __uint_as_float(u[c][2 * e])),
-                                    silu_gate(__uint_as_float(g[c][2 * e + 1]),
-                                              __uint_as_float(u[c][2 * e + 1])));
-      #pragma unroll
-      for (int e = 8 * kC16; e < 32; ++e) w[e] = 0u;
+        for (int c = 0; c < 2; ++c) {
+          tmem_ld_32x32b_x32(t_gate + 32 * c, g[c]);
+          tmem_ld_32x32b_x32(t_up + 32 * c, u[c]);
+        }
+        tmem_ld_wait();
+        #pragma unroll
+        for (int c = 0; c < 2; ++c) tmem_regs_ready(g[c]), tmem_regs_ready(u[c]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(acc_empty_leader);
+        #pragma unroll
+        for (int c = 0; c < 2; ++c)
+          #pragma unroll
+          for (int e = 0; e < 16; ++e)
+            w[16 * c + e] = pack_half2(silu_gate(__uint_as_float(g[c][2 * e]), __uint_as_float(u[c][2 * e])),
+                                       silu_gate(__uint_as_float(g[c][2 * e + 1]),
+                                                 __uint_as_float(u[c][2 * e + 1])));
+      } else {
+        uint32_t g[kC16][16], u[kC16][16];
+        #pragma unroll
+        for (int c = 0; c < kC16; ++c) {
+          tmem_ld_32x32b_x16(t_gate + 16 * c, g[c]);
+          tmem_ld_32x32b_x16(t_up + 16 * c, u[c]);
+        }
+        tmem_ld_wait();
+        #pragma unroll
+        for (int c = 0; c < kC16; ++c) tmem_regs_ready16(g[c]), tmem_regs_ready16(u[c]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(acc_empty_leader);
+        #pragma unroll
+        for (int c = 0; c < kC16; ++c)
+          #pragma unroll
+          for (int e = 0; e < 8; ++e)
+            w[8 * c + e] = pack_half2(silu_gate(__uint_as_float(g[c][2 * e]), __uint_as_float(u[c][2 * e])),
+                                      silu_gate(__uint_as_float(g[c][2 * e + 1]),
+                                                __uint_as_float(u[c][2 * e + 1])));
+        #pragma unroll
+        for (int e = 8 * kC16; e < 32; ++e) w[e] = 0u;
+      }
+      acc_phase ^= 1u;
       // kCW columns per row (48: three 32-byte chunks of a line, 64: a line)
       const int row0 = tc.mp * 2 * kBM + (int)rank * kBM + quad * 32;
       const int col0 = tc.nb * Cfg::kBN + kCW * part;
