@@ -111,6 +111,27 @@ def quant_workload(rank, world, device):
     return xs, 0.0, nbytes, desc
 
 
+def moe_workload(rank, world, device):
+    """Configuration 6: MoE dispatch of configuration 4's routing (32768 tokens,
+    Zipf over 64 experts, top-1) at its K = 7168: fp32 tokens -> per-expert
+    NVFP4 A operands + scale atoms + permutation; HBM-bound."""
+    from nvfp4_b200 import inputs as I
+    from nvfp4_b200 import moe
+    spec = I.GROUP_CONFIGS[4]
+    tokens, k, experts = 32768, spec["k"], 64
+    g = torch.Generator().manual_seed(4000 + rank)
+    x = torch.randn(tokens, k, generator=g).to(device)
+    ids = I.config4_expert_ids(seed=4 + rank).to(device)
+    d = moe.dispatch(x, ids, experts)                  # buffers allocated once, reused per step
+    torch.cuda.synchronize()
+    blocks = int(d.atom_offsets[-1].item())
+    rows = int(d.row_offsets[-1].item())
+    nbytes = (tokens * k * 4 + tokens * 4 + rows * k // 2 + blocks * (k // 64) * 512
+              + 2 * rows * 4 + 3 * (experts + 1) * 4)
+    desc = dict(workload="moe_dispatch_cfg4", tokens=tokens, k=k, experts=experts, topk=1)
+    return (x, ids, experts, d), 0.0, nbytes, desc
+
+
 def shape_workload(args, device):
     """--shape M,N,K (dual) or --group-shape M1:M2:..,N,K (grouped): a seeded
     N(0,1) workload of any size for kernel-only profiling runs."""
@@ -134,6 +155,8 @@ def shape_workload(args, device):
 def make_workload(cfg, rank, world, device):
     if cfg == 5:
         return quant_workload(rank, world, device)
+    if cfg == 6:
+        return moe_workload(rank, world, device)
     return dual_workload(cfg, rank, world, device) if cfg in (0, 1, 2) else \
         group_workload(cfg, rank, world, device)
 
@@ -142,6 +165,10 @@ def call(cfg, data):
     if cfg == 5:
         from nvfp4_b200.quantize import quantize
         return [quantize(x, out=o) for x, o in data]
+    if cfg == 6:
+        from nvfp4_b200 import moe
+        x, ids, experts, d = data
+        return moe.dispatch(x, ids, experts, out=d)
     if cfg in (0, 1, 2):
         from nvfp4_b200.dual_gemm import custom_kernel
     else:
@@ -153,6 +180,9 @@ def device_tensors(cfg, data):
     """(input tensors a user would ship each step, output tensors)."""
     if cfg == 5:
         return [x for x, _ in data], [t for _, o in data for t in o]
+    if cfg == 6:
+        x, ids, _, d = data
+        return [x, ids], [d.packed, d.sf, d.counts, d.row_offsets, d.atom_offsets, d.src, d.dst]
     if cfg in (0, 1, 2):
         return [data[0], data[1], data[2], data[6], data[7], data[8]], [data[9]]
     abc, _, perm, sizes = data
@@ -301,6 +331,27 @@ def time_cpu_quant(x_dev, budget_s: float):
                       f"(~{budget_s:.0f} s, single-threaded numpy)"}
 
 
+def time_cpu_moe(x_dev, ids_dev, experts, budget_s: float):
+    """Oracle dispatch (numpy) on the first 1024 tokens, bytes counted as on
+    the device: fp32 tokens + ids in, e2m1 rows + scale atoms + src/dst out."""
+    from oracle import nvfp4_oracle as O
+    x = x_dev[:1024].detach().cpu().numpy()
+    ids = ids_dev[:1024].detach().cpu().numpy().reshape(-1, 1)
+    t, k = x.shape
+    (_, _, atom_off, _, _), _, _ = O.moe_dispatch(x[:16], ids[:16], experts)
+    (_, _, atom_off, _, _), _, _ = O.moe_dispatch(x, ids, experts)
+    nb = t * k * 4 + t * 4 + t * k // 2 + int(atom_off[-1]) * (k // 64) * 512 + 2 * t * 4
+    secs, reps = 0.0, 0
+    while reps < 1 or secs < budget_s:
+        t0 = time.perf_counter()
+        O.moe_dispatch(x, ids, experts)
+        secs += time.perf_counter() - t0
+        reps += 1
+    return {"value": round(nb * reps / secs / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"numpy oracle dispatch (route + quantise + swizzle) of {t} tokens x K={k}, "
+                      f"{reps} reps (~{budget_s:.0f} s, single-threaded numpy)"}
+
+
 def cpu_cores():
     try:
         return len(os.sched_getaffinity(0))
@@ -422,6 +473,8 @@ def run_task_suite(args):
 def metric_name(cfg):
     if cfg == 5:
         return "NVFP4 quantisation bandwidth (fp32 -> e2m1 + e4m3 scales)"
+    if cfg == 6:
+        return "MoE dispatch bandwidth (route + fp32 -> NVFP4 per-expert operands)"
     return "NVFP4 effective TFLOPS (dual GEMM)" if cfg in (0, 1, 2) else \
         "NVFP4 effective TFLOPS (grouped GEMM)"
 
@@ -431,8 +484,9 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4, 5],
-                    help="0-4: BASELINE configurations; 5: device quantisation of config 1's operands")
+    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4, 5, 6],
+                    help="0-4: BASELINE configurations; 5: device quantisation of config 1's "
+                         "operands; 6: MoE dispatch of config 4's routing")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
@@ -509,7 +563,7 @@ def main():
     t_max_s = t_total.item() / 1e3
     total_flop = flop_t.item() * args.steps
     ms_per_step = t_max_s * 1e3 / args.steps
-    if cfg == 5:   # bytes-moved metric for the quantiser
+    if cfg in (5, 6):   # bytes-moved metric for the quantiser and the dispatch
         bytes_t = torch.tensor([float(nbytes)], dtype=torch.float64, device=device)
         if pg:
             pg.all_reduce(bytes_t, op=pg.ReduceOp.SUM)
@@ -520,7 +574,7 @@ def main():
     if args.kernel_only:
         if rank == 0:
             print(json.dumps({"metric": metric_name(cfg), "value": round(value, 2),
-                              "unit": "GB/s" if cfg == 5 else "TFLOP/s",
+                              "unit": "GB/s" if cfg in (5, 6) else "TFLOP/s",
                               "us_per_call": round(ms_per_step * 1e3, 2),
                               "config": desc, "kernel_only": True, "clocks": clk.summary()}),
                   flush=True)
@@ -551,8 +605,8 @@ def main():
     e2e_t = torch.tensor([es.elapsed_time(ee) / 1e3], dtype=torch.float64, device=device)
     if pg:
         pg.all_reduce(e2e_t, op=pg.ReduceOp.MAX)
-    quant = cfg == 5
-    if quant:   # bytes-moved metric for the quantiser
+    quant = cfg in (5, 6)
+    if quant:   # bytes-moved metric for the quantiser and the dispatch
         e2e_value = bytes_t.item() * args.e2e_steps / e2e_t.item() / 1e9
     else:
         e2e_value = flop_t.item() * args.e2e_steps / e2e_t.item() / 1e12
@@ -562,7 +616,7 @@ def main():
     hbm_peak, bf16_peak, peak_kind = load_peaks()
     nvfp4_peak = 4.0 * bf16_peak
     avg_launch_s = statistics.mean(per_call_ms) / 1e3
-    hbm_bound = cfg in (2, 5)
+    hbm_bound = cfg in (2, 5, 6)
     traffic = load_traffic(desc["workload"])
     if hbm_bound:
         ach = nbytes / avg_launch_s / 1e9
@@ -581,22 +635,25 @@ def main():
         "metric": metric_name(cfg), "value": round(value, 2), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 5), "us_per_call": round(ms_per_step * 1e3, 2),
-        "higher_is_better": True, "scaling": "weak" if cfg in (0, 1, 2) else "strong",
+        "higher_is_better": True, "scaling": "weak" if cfg in (0, 1, 2, 6) else "strong",
         "vs_baseline": None,
-        "dtype": "fp32 -> e2m1 + e4m3 block16" if quant
+        "dtype": ("int32 routing + fp32 -> e2m1 + e4m3 block16" if cfg == 6 else
+                  "fp32 -> e2m1 + e4m3 block16") if quant
         else "nvfp4(e2m1+e4m3 block16) x nvfp4 -> fp32 acc -> fp16",
         "data": "synthetic: seeded N(0,1) fp32 quantised to NVFP4",
-        "config": {**desc, "parallelism": f"{'n-shard' if cfg in (0, 1, 2) else 'expert-lpt'}{world}",
+        "config": {**desc, "parallelism": f"{'n-shard' if cfg in (0, 1, 2) else 'token-shard' if cfg == 6 else 'expert-lpt'}{world}",
                    "l2": f"flushed ({L2_FLUSH_BYTES >> 20} MiB write) between timed calls"},
         "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
                 "api": "nvfp4_b200.*.custom_kernel (ctypes -> libnvfp4_b200.so)"},
         "roofline": roof,
-        "gpu_launches": args.steps * (len(data) if quant else 1),
+        "gpu_launches": args.steps * (4 if cfg == 6 else len(data) if quant else 1),
         "clocks": clk.summary(),
     }
 
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and quant:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and cfg == 6:
+        result["cpu_baseline"] = time_cpu_moe(data[0], data[1], data[2], args.cpu_budget)
+    elif rank == 0 and world == 1 and not args.no_cpu_baseline and quant:
         result["cpu_baseline"] = time_cpu_quant(data[0][0], args.cpu_budget)
     elif rank == 0 and world == 1 and not args.no_cpu_baseline:
         dc = cpu_inputs(cfg, data)
@@ -619,6 +676,8 @@ def run_reference_arm(args, cfg, rank, world):
     if rank != 0:
         return
     from nvfp4_b200 import inputs as I
+    if cfg in (5, 6):
+        return run_reference_bytes_arm(args, cfg, world)
     if cfg in (0, 1, 2):
         spec = I.DUAL_CONFIGS[cfg]
         g = torch.Generator().manual_seed(spec["seed"])
@@ -664,6 +723,36 @@ def run_reference_arm(args, cfg, rank, world):
         "cpu_baseline": {"value": round(v, 5), "unit": "TFLOP/s", "cores": cpu_cores(),
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(v, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_reference_bytes_arm(args, cfg, world):
+    """Configurations 5 and 6 on the host: the numpy oracle quantiser / dispatch
+    (the reference has no such step; its inputs are built on the host) on a
+    1024-row sample per step, GB/s counted as on the device."""
+    from nvfp4_b200 import inputs as I
+    g = torch.Generator().manual_seed(5)
+    budget = max(0.5, 150.0 / max(1, args.steps))
+    if cfg == 5:
+        x = torch.randn(1024, I.DUAL_CONFIGS[1]["k"], generator=g)
+        runs = [time_cpu_quant(x, budget) for _ in range(args.steps)]
+        wl = "quantize_cfg1_operands"
+    else:
+        x = torch.randn(1024, I.GROUP_CONFIGS[4]["k"], generator=g)
+        ids = I.config4_expert_ids()[:1024]
+        runs = [time_cpu_moe(x, ids, 64, budget) for _ in range(args.steps)]
+        wl = "moe_dispatch_cfg4"
+    v = statistics.mean(r["value"] for r in runs)
+    print(json.dumps({
+        "impl": "reference", "metric": metric_name(cfg), "value": round(v, 4), "unit": "GB/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(budget * 1e3, 1), "higher_is_better": True,
+        "scaling": "weak" if cfg == 6 else "strong", "vs_baseline": None,
+        "dtype": "fp32 -> e2m1 + e4m3 block16", "data": "synthetic: seeded N(0,1) fp32",
+        "config": {"workload": wl, "sample_rows": 1024, "budget_s": budget},
+        "cpu_baseline": {**runs[0], "value": round(v, 4)},
+        "e2e": {"value": round(v, 4), "unit": "GB/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
 

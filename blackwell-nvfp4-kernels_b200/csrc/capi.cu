@@ -19,6 +19,7 @@
 #include "dual_gemm_2sm.cuh"
 #include "grouped_gemm.cuh"
 #include "quantize.cuh"
+#include "moe.cuh"
 
 namespace nvfp4 {
 
@@ -658,6 +659,119 @@ extern "C" int nvfp4_quantize(const float* x, int rows, int k, int l, void* pack
   const dim3 grid(p.k_atoms, row_blocks, l);
   quantize_nvfp4_kernel<<<grid, kQuantThreads, 0, static_cast<cudaStream_t>(stream_)>>>(p);
   return check_launch("quantize_nvfp4_kernel");
+}
+
+// ---------------------------------------------------------------------------
+// MoE dispatch (route -> per-expert NVFP4 A operands) and combine.
+// ---------------------------------------------------------------------------
+extern "C" size_t nvfp4_moe_workspace_bytes(int tokens, int topk, int num_experts) {
+  if (tokens < 0 || topk < 1 || num_experts < 1) return 0;
+  const long long pairs = (long long)tokens * topk;
+  const long long chunks = (pairs + kMoeChunk - 1) / kMoeChunk;
+  return (size_t)(chunks > 0 ? chunks : 1) * (size_t)num_experts * sizeof(int);
+}
+
+extern "C" size_t nvfp4_moe_sf_bytes(int tokens, int topk, int k, int num_experts) {
+  if (tokens < 0 || topk < 1 || num_experts < 1 || k < 64) return 0;
+  const long long pairs = (long long)tokens * topk;
+  const long long blocks = (pairs + 127) / 128 + (pairs < num_experts ? pairs : num_experts);
+  return (size_t)blocks * (size_t)(k / 64) * 512u;
+}
+
+extern "C" int nvfp4_moe_dispatch(const float* x, const int* expert_ids, int tokens, int topk,
+                                  int k, int num_experts, void* packed, void* sf_perm, int* counts,
+                                  int* row_offsets, int* atom_offsets, int* src, int* dst,
+                                  void* workspace, size_t workspace_bytes, void* stream_) {
+  if (tokens < 0 || topk < 1 || k < 1 || num_experts < 1)
+    return fail(NVFP4_ERR_INVALID_ARG, "bad sizes (tokens=%d topk=%d k=%d experts=%d)", tokens,
+                topk, k, num_experts);
+  if (num_experts > kMoeMaxExperts)
+    return fail(NVFP4_ERR_SHAPE, "%d experts (at most %d)", num_experts, kMoeMaxExperts);
+  if (k % 64 != 0) return fail(NVFP4_ERR_SHAPE, "K=%d is not a multiple of 64", k);
+  const long long pairs = (long long)tokens * topk;
+  const long long max_blocks = (pairs + 127) / 128 + (pairs < num_experts ? pairs : num_experts);
+  if (pairs >= (1LL << 31) / 2 || max_blocks > 65535 || pairs * (long long)k >= (1LL << 40))
+    return fail(NVFP4_ERR_SHAPE, "problem too large");
+  if (!counts || !row_offsets || !atom_offsets || !workspace ||
+      (pairs > 0 && (!x || !expert_ids || !packed || !sf_perm || !src || !dst)))
+    return fail(NVFP4_ERR_INVALID_ARG, "null pointer argument");
+  if (workspace_bytes < nvfp4_moe_workspace_bytes(tokens, topk, num_experts))
+    return fail(NVFP4_ERR_INVALID_ARG, "workspace too small (%zu < %zu bytes)", workspace_bytes,
+                nvfp4_moe_workspace_bytes(tokens, topk, num_experts));
+  if ((x && !aligned16(x)) || (packed && !aligned16(packed)) || (sf_perm && !aligned16(sf_perm)) ||
+      (reinterpret_cast<uintptr_t>(workspace) & 3u))
+    return fail(NVFP4_ERR_ALIGNMENT, "x/packed/sf_perm need 16-byte alignment");
+  DeviceState* d = nullptr;
+  int rc = get_device(&d);
+  if (rc) return rc;
+  const cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  MoeParams p;
+  p.x = x, p.ids = expert_ids;
+  p.pairs = (int)pairs, p.topk = topk, p.k = k, p.experts = num_experts;
+  p.chunks = (int)((pairs + kMoeChunk - 1) / kMoeChunk);
+  p.k_atoms = k / 64;
+  p.chunk_counts = static_cast<int*>(workspace);
+  p.counts = counts, p.row_offsets = row_offsets, p.atom_offsets = atom_offsets;
+  p.src = src, p.dst = dst;
+  p.packed = static_cast<uint8_t*>(packed);
+  p.sf_perm = static_cast<uint8_t*>(sf_perm);
+  const size_t hist_bytes = (size_t)kMoeWarps * num_experts * sizeof(int);
+  const int chunk_ctas = (p.chunks + kMoeWarps - 1) / kMoeWarps;
+  if (chunk_ctas > 0) {
+    moe_count_kernel<<<chunk_ctas, 32 * kMoeWarps, hist_bytes, stream>>>(p);
+    if ((rc = check_launch("moe_count_kernel"))) return rc;
+  }
+  const int scan_threads = (num_experts + 31) / 32 * 32;
+  moe_scan_kernel<<<1, scan_threads, 0, stream>>>(p);
+  if ((rc = check_launch("moe_scan_kernel"))) return rc;
+  if (chunk_ctas > 0) {
+    moe_scatter_kernel<<<chunk_ctas, 32 * kMoeWarps, hist_bytes, stream>>>(p);
+    if ((rc = check_launch("moe_scatter_kernel"))) return rc;
+    const dim3 grid(p.k_atoms, (unsigned)max_blocks, 1);
+    moe_quantize_kernel<<<grid, kQuantThreads, 0, stream>>>(p);
+    if ((rc = check_launch("moe_quantize_kernel"))) return rc;
+  }
+  return NVFP4_OK;
+}
+
+extern "C" int nvfp4_moe_combine(const void* c, int c_rows, const int* dst, const float* weights,
+                                 int tokens, int topk, int n, float* out, void* stream_) {
+  if (tokens < 0 || topk < 1 || n < 1 || c_rows < 0)
+    return fail(NVFP4_ERR_INVALID_ARG, "bad sizes (tokens=%d topk=%d n=%d c_rows=%d)", tokens,
+                topk, n, c_rows);
+  if (tokens == 0) return NVFP4_OK;
+  if (!c || !dst || !out) return fail(NVFP4_ERR_INVALID_ARG, "null pointer argument");
+  if ((long long)tokens > 65535 * 1024LL || (long long)tokens * n >= (1LL << 40))
+    return fail(NVFP4_ERR_SHAPE, "problem too large");
+  if ((reinterpret_cast<uintptr_t>(c) & 1u) || (reinterpret_cast<uintptr_t>(out) & 3u) ||
+      (reinterpret_cast<uintptr_t>(dst) & 3u) || (weights && (reinterpret_cast<uintptr_t>(weights) & 3u)))
+    return fail(NVFP4_ERR_ALIGNMENT, "c needs 2-byte, dst/weights/out 4-byte alignment");
+  DeviceState* d = nullptr;
+  int rc = get_device(&d);
+  if (rc) return rc;
+  MoeCombineParams p;
+  p.c = static_cast<const __half*>(c);
+  p.dst = dst, p.w = weights, p.out = out;
+  p.tokens = tokens, p.topk = topk, p.n = n, p.c_rows = c_rows;
+  const int span = kCombineThreads * 8;
+  const cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const bool vec = n % 8 == 0 && aligned16(c) && aligned16(out);
+  // grid.y is limited to 65535: token rows beyond it go in further launches
+  for (int t0 = 0; t0 < tokens; t0 += 65535) {
+    MoeCombineParams q = p;
+    const int nt = tokens - t0 < 65535 ? tokens - t0 : 65535;
+    q.dst = p.dst + (size_t)t0 * topk;
+    q.w = p.w ? p.w + (size_t)t0 * topk : nullptr;
+    q.out = p.out + (size_t)t0 * n;
+    q.tokens = nt;
+    const dim3 grid((n + span - 1) / span, nt, 1);
+    if (vec)
+      moe_combine_kernel<true><<<grid, kCombineThreads, 0, stream>>>(q);
+    else
+      moe_combine_kernel<false><<<grid, kCombineThreads, 0, stream>>>(q);
+    if ((rc = check_launch("moe_combine_kernel"))) return rc;
+  }
+  return NVFP4_OK;
 }
 
 // ---------------------------------------------------------------------------

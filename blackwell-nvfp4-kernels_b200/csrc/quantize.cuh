@@ -50,24 +50,27 @@ __device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
 // 4-byte word of the scale atom (byte (r%32)*16 + ((r/32)%4)*4 + block).
 constexpr int kQuantThreads = 256;
 
-__global__ void __launch_bounds__(kQuantThreads) quantize_nvfp4_kernel(const QuantParams p) {
-  const int atom = blockIdx.x;                 // k-atom index (64 K per atom)
-  const int rb = blockIdx.y;                   // 128-row block
-  const int l = blockIdx.z;
+// The body shared by the plain quantiser and the MoE gather-quantiser: rows
+// r = 0..127 of one 128-row block, one 64-deep K atom.  src(r) -> the fp32
+// row (nullptr past the block's valid rows), packed(r) -> the packed row,
+// plain(r) -> the plain-scale row or nullptr; atom_base -> the block's
+// 512-byte scale atom for this K atom (padding rows get zero scales).
+template <class Src, class Packed, class Plain>
+__device__ __forceinline__ void quantize_atom_block(int atom, uint8_t* atom_base, Src src,
+                                                    Packed packed, Plain plain) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane & 7;                    // which 8 values of the 64-value row segment
-  uint8_t* atom_base = p.sf_perm + (((size_t)l * p.row_blocks + rb) * p.k_atoms + atom) * 512;
   constexpr int kSteps = 128 / (4 * (kQuantThreads / 32));
   // all of this thread's loads first (4 x 32 bytes in flight per lane)
   float v[kSteps][8];
+  const float* row_src[kSteps];
   #pragma unroll
   for (int step = 0; step < kSteps; ++step) {
     const int r = (step * (kQuantThreads / 32) + warp) * 4 + (lane >> 3);
-    const int row = rb * 128 + r;
-    if (row < p.rows) {
-      const float4* src = reinterpret_cast<const float4*>(
-          p.x + ((size_t)l * p.rows + row) * (size_t)p.k + (size_t)atom * 64 + 8 * sub);
-      const float4 f0 = __ldcs(src), f1 = __ldcs(src + 1);
+    row_src[step] = src(r);
+    if (row_src[step] != nullptr) {
+      const float4* q = reinterpret_cast<const float4*>(row_src[step] + (size_t)atom * 64 + 8 * sub);
+      const float4 f0 = __ldcs(q), f1 = __ldcs(q + 1);
       v[step][0] = f0.x, v[step][1] = f0.y, v[step][2] = f0.z, v[step][3] = f0.w;
       v[step][4] = f1.x, v[step][5] = f1.y, v[step][6] = f1.z, v[step][7] = f1.w;
     } else {
@@ -78,8 +81,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_nvfp4_kernel(const Qua
   #pragma unroll
   for (int step = 0; step < kSteps; ++step) {
     const int r = (step * (kQuantThreads / 32) + warp) * 4 + (lane >> 3);   // row in the block
-    const int row = rb * 128 + r;
-    const bool valid = row < p.rows;
+    const bool valid = row_src[step] != nullptr;
     float amax = 0.f;
     #pragma unroll
     for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[step][e]));
@@ -100,16 +102,28 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_nvfp4_kernel(const Qua
     for (int b = 0; b < 4; ++b)
       sf_word |= (__shfl_sync(0xffffffffu, (uint32_t)s8, row_lane0 + 2 * b) & 0xffu) << (8 * b);
     if (valid) {
-      *reinterpret_cast<uint32_t*>(p.packed + ((size_t)l * p.rows + row) * (size_t)(p.k / 2) +
-                                   (size_t)atom * 32 + 4 * sub) = word;
-      if (sub == 0 && p.sf_plain)
-        *reinterpret_cast<uint32_t*>(p.sf_plain + ((size_t)l * p.rows + row) * (size_t)(p.k / 16) +
-                                     (size_t)atom * 4) = sf_word;
+      *reinterpret_cast<uint32_t*>(packed(r) + (size_t)atom * 32 + 4 * sub) = word;
+      uint8_t* pl = plain(r);
+      if (sub == 0 && pl != nullptr) *reinterpret_cast<uint32_t*>(pl + (size_t)atom * 4) = sf_word;
     }
-    // rows past `rows` leave zero scales in the atom's padding
+    // rows past the valid ones leave zero scales in the atom's padding
     if (sub == 0)
       *reinterpret_cast<uint32_t*>(atom_base + (r % 32) * 16 + (r / 32) * 4) = valid ? sf_word : 0u;
   }
+}
+
+__global__ void __launch_bounds__(kQuantThreads) quantize_nvfp4_kernel(const QuantParams p) {
+  const int atom = blockIdx.x;                 // k-atom index (64 K per atom)
+  const int rb = blockIdx.y;                   // 128-row block
+  const int l = blockIdx.z;
+  uint8_t* atom_base = p.sf_perm + (((size_t)l * p.row_blocks + rb) * p.k_atoms + atom) * 512;
+  const size_t row0 = (size_t)l * p.rows + (size_t)rb * 128;
+  const int valid_rows = min(128, p.rows - rb * 128);
+  quantize_atom_block(
+      atom, atom_base,
+      [&](int r) -> const float* { return r < valid_rows ? p.x + (row0 + r) * (size_t)p.k : nullptr; },
+      [&](int r) -> uint8_t* { return p.packed + (row0 + r) * (size_t)(p.k / 2); },
+      [&](int r) -> uint8_t* { return p.sf_plain ? p.sf_plain + (row0 + r) * (size_t)(p.k / 16) : nullptr; });
 }
 
 }  // namespace nvfp4

@@ -25,6 +25,10 @@ EXPORTED = (
     "nvfp4_dual_gemm_noalloc",
     "nvfp4_grouped_gemm",
     "nvfp4_quantize",
+    "nvfp4_moe_dispatch",
+    "nvfp4_moe_workspace_bytes",
+    "nvfp4_moe_sf_bytes",
+    "nvfp4_moe_combine",
     "nvfp4_device_status",
     "nvfp4_wait_selftest",
     "nvfp4_status_string",
@@ -77,6 +81,16 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
     lib.nvfp4_grouped_gemm.restype = i32
     lib.nvfp4_quantize.argtypes = [vp, i32, i32, i32, vp, vp, vp, vp]
     lib.nvfp4_quantize.restype = i32
+    sz = ctypes.c_size_t
+    lib.nvfp4_moe_dispatch.argtypes = [vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp, vp,
+                                       vp, sz, vp]
+    lib.nvfp4_moe_dispatch.restype = i32
+    lib.nvfp4_moe_workspace_bytes.argtypes = [i32, i32, i32]
+    lib.nvfp4_moe_workspace_bytes.restype = sz
+    lib.nvfp4_moe_sf_bytes.argtypes = [i32, i32, i32, i32]
+    lib.nvfp4_moe_sf_bytes.restype = sz
+    lib.nvfp4_moe_combine.argtypes = [vp, i32, vp, vp, i32, i32, i32, vp, vp]
+    lib.nvfp4_moe_combine.restype = i32
     lib.nvfp4_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint)]
     lib.nvfp4_device_status.restype = i32
     lib.nvfp4_wait_selftest.argtypes = [ctypes.c_longlong, vp]

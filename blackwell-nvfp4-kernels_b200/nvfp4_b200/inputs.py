@@ -38,16 +38,23 @@ def config3_m_sizes(seed: int = 1, groups: int = 8) -> list[int]:
     return [int(v) * 64 for v in torch.randint(1, 33, (groups,), generator=g)]
 
 
-def config4_m_sizes(seed: int = 4, experts: int = 64, tokens: int = 32768,
-                    s: float = 1.1) -> list[int]:
-    """Zipf(s) routing of `tokens` tokens over `experts` experts: rank r in
-    1..experts has weight r**-s, ranks map to experts by a seeded permutation,
-    tokens draw experts by seeded multinomial sampling with replacement."""
+def config4_expert_ids(seed: int = 4, experts: int = 64, tokens: int = 32768,
+                       s: float = 1.1) -> torch.Tensor:
+    """Zipf(s) routing of `tokens` tokens over `experts` experts (int32 [tokens]):
+    rank r in 1..experts has weight r**-s, ranks map to experts by a seeded
+    permutation, tokens draw experts by seeded multinomial sampling with
+    replacement."""
     g = torch.Generator().manual_seed(seed)
     w = torch.arange(1, experts + 1, dtype=torch.float64) ** (-s)
     perm = torch.randperm(experts, generator=g)
     ranks = torch.multinomial(w, tokens, replacement=True, generator=g)
-    expert = perm[ranks]
+    return perm[ranks].to(torch.int32)
+
+
+def config4_m_sizes(seed: int = 4, experts: int = 64, tokens: int = 32768,
+                    s: float = 1.1) -> list[int]:
+    """Tokens per expert of :func:`config4_expert_ids` (configuration 4's M_g)."""
+    expert = config4_expert_ids(seed, experts, tokens, s).long()
     return [int(v) for v in torch.bincount(expert, minlength=experts)]
 
 

@@ -20,6 +20,7 @@
 #ifndef NVFP4_B200_H
 #define NVFP4_B200_H
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -84,6 +85,46 @@ int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream);
  * construction of nvfp4_dual_gemm/reference.py:113-187 moved on-device. */
 int nvfp4_quantize(const float* x, int rows, int k, int l, void* packed, void* sf_perm,
                    void* sf_plain, void* stream);
+
+/* MoE dispatch: routes `tokens` fp32 rows x [tokens][K] (K % 64 == 0, 16-byte
+ * aligned) with `topk` expert choices each, expert_ids[t*topk + j] (choices
+ * outside [0, num_experts) are dropped; num_experts <= 1024), into the
+ * per-expert NVFP4 A operands of nvfp4_grouped_gemm, on the device:
+ *   counts[e]            pairs routed to expert e
+ *   row_offsets[e]       sum of counts[e' < e]; row_offsets[E] = rows used
+ *   atom_offsets[e]      sum of ceil(counts[e'] / 128) for e' < e
+ *   src[row]             pair index t*topk + j held by permuted row `row`
+ *                        (rows of one expert in ascending pair order)
+ *   dst[t*topk + j]      permuted row of that pair, -1 if dropped
+ *   packed               [tokens*topk][K/2] e2m1 bytes, row r = x[src[r]/topk]
+ *                        quantised exactly as nvfp4_quantize does
+ *   sf_perm              expert e's permuted scale atoms [ceil(counts[e]/128)]
+ *                        [K/64][512] from byte atom_offsets[e]*(K/64)*512
+ *                        (padding rows zero); size nvfp4_moe_sf_bytes()
+ * so that expert e's grouped-GEMM operand is A = packed + row_offsets[e]*K/2,
+ * SFA = sf_perm + atom_offsets[e]*(K/64)*512, M = counts[e].  `workspace`
+ * (nvfp4_moe_workspace_bytes(), 4-byte aligned) is scratch owned by the
+ * call until it completes on `stream`.  Asynchronous; offsets stay on the
+ * device.  No reference counterpart: the reference's grouped GEMM
+ * (nvfp4_group_gemm/reference.py:39-74) takes the per-expert A_g as given;
+ * this is the routing step that produces them. */
+int nvfp4_moe_dispatch(const float* x, const int* expert_ids, int tokens, int topk, int k,
+                       int num_experts, void* packed, void* sf_perm, int* counts,
+                       int* row_offsets, int* atom_offsets, int* src, int* dst, void* workspace,
+                       size_t workspace_bytes, void* stream);
+size_t nvfp4_moe_workspace_bytes(int tokens, int topk, int num_experts);
+/* Upper bound of the dispatch's scale bytes: (ceil(tokens*topk/128) +
+ * min(num_experts, tokens*topk)) * (K/64) * 512. */
+size_t nvfp4_moe_sf_bytes(int tokens, int topk, int k, int num_experts);
+
+/* MoE combine: out[t][n] = sum over j of weights[t*topk + j] *
+ * c[dst[t*topk + j]][n] (fp32, j ascending, products and sums rounded
+ * separately; pairs with dst < 0 or dst >= c_rows skipped; weights == NULL
+ * means 1), with c the fp16 [c_rows][N] output of the grouped GEMM over the
+ * dispatch's permuted rows and dst the dispatch's dst.  No reference
+ * counterpart. */
+int nvfp4_moe_combine(const void* c, int c_rows, const int* dst, const float* weights, int tokens,
+                      int topk, int n, float* out, void* stream);
 
 /* Synchronises `stream`, then reads and clears this device's status word.
  * Returns NVFP4_ERR_TIMEOUT if a kernel gave up on a wait (bits in *bits_out,

@@ -112,3 +112,28 @@ def test_sf_layout_validation():
     bad = pa.contiguous()   # logical-order contiguous: not the atom memory image
     with pytest.raises(ValueError, match="strides"):
         D.check_sf_perm("sfa", bad, 256, 256, 1, bad.device)
+
+
+def test_moe_sizes_and_rejections_without_gpu(lib):
+    # workspace: one int per (chunk of 1024 pairs, expert); scales: upper bound of 128-row blocks
+    assert lib.nvfp4_moe_workspace_bytes(32768, 1, 64) == 32 * 64 * 4
+    assert lib.nvfp4_moe_workspace_bytes(0, 1, 8) == 8 * 4
+    assert lib.nvfp4_moe_sf_bytes(32768, 1, 7168, 64) == (256 + 64) * 112 * 512
+    assert lib.nvfp4_moe_sf_bytes(3, 2, 64, 64) == (1 + 6) * 1 * 512
+    p = ctypes.c_void_p(4096)
+    ws = lib.nvfp4_moe_workspace_bytes(100, 2, 8)
+    f = lib.nvfp4_moe_dispatch
+    assert f(p, p, 100, 2, 100, 8, p, p, p, p, p, p, p, p, ws, None) == _lib.NVFP4_ERR_SHAPE
+    assert f(p, p, 100, 2, 128, 2000, p, p, p, p, p, p, p, p, ws, None) == _lib.NVFP4_ERR_SHAPE
+    assert f(p, p, 100, 0, 128, 8, p, p, p, p, p, p, p, p, ws, None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert f(None, p, 100, 2, 128, 8, p, p, p, p, p, p, p, p, ws, None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert f(p, p, 100, 2, 128, 8, p, p, p, p, p, p, p, p, ws - 4, None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert b"workspace" in lib.nvfp4_last_error()
+    q = ctypes.c_void_p(4096 + 4)
+    assert f(q, p, 100, 2, 128, 8, p, p, p, p, p, p, p, p, ws, None) == _lib.NVFP4_ERR_ALIGNMENT
+    g = lib.nvfp4_moe_combine
+    assert g(p, 10, p, None, 10, 0, 64, p, None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert g(p, -1, p, None, 10, 1, 64, p, None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert g(None, 10, p, None, 10, 1, 64, p, None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert g(p, 10, p, None, 0, 1, 64, p, None) == _lib.NVFP4_OK      # nothing to combine
+    assert g(ctypes.c_void_p(4097), 10, p, None, 10, 1, 64, p, None) == _lib.NVFP4_ERR_ALIGNMENT
