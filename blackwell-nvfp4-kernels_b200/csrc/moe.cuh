@@ -177,14 +177,16 @@ __global__ void __launch_bounds__(32 * kMoeWarps) moe_scatter_kernel(const MoePa
 __global__ void __launch_bounds__(kQuantThreads) moe_quantize_kernel(const MoeParams p) {
   const int atom = blockIdx.x;
   const int gb = blockIdx.y;                          // 128-row block over all experts
-  if (gb >= p.atom_offsets[p.experts]) return;
-  // the expert owning block gb: the last e with atom_offsets[e] <= gb
-  int lo = 0, hi = p.experts - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (p.atom_offsets[mid] <= gb) lo = mid; else hi = mid - 1;
-  }
-  const int e = lo;
+  // the expert owning block gb (atom_offsets[e] <= gb < atom_offsets[e + 1]):
+  // every thread tests a few experts, one dependent load instead of a search
+  __shared__ int s_expert;
+  if (threadIdx.x == 0) s_expert = -1;
+  __syncthreads();
+  for (int i = threadIdx.x; i < p.experts; i += blockDim.x)
+    if (__ldg(p.atom_offsets + i) <= gb && gb < __ldg(p.atom_offsets + i + 1)) s_expert = i;
+  __syncthreads();
+  const int e = s_expert;
+  if (e < 0) return;                                  // past the last block: whole CTA exits
   const int local_block = gb - p.atom_offsets[e];
   const int row0 = p.row_offsets[e] + local_block * 128;
   const int valid_rows = min(128, p.row_offsets[e + 1] - row0);

@@ -109,3 +109,29 @@ def test_dual_config0_quantisation_matches_oracle():
     pa, sa = O.quantize_nvfp4(a.numpy())
     assert np.array_equal(d[0].view(torch.uint8)[:, :, 0].numpy(), pa)
     assert np.array_equal(d[3].view(torch.uint8)[:, :, 0].numpy(), sa)
+
+
+def test_reciprocal_fma_quotient_is_ieee_division():
+    """The device quantiser forms x / s without a division: r = RN(1/s),
+    q0 = RN(x*r), q1 = RN(q0 + RN(x - q0*s) * r) (two FMAs).  Exhaustive
+    check that q1 == RN(x/s) for every fp32 mantissa of x and every e4m3
+    scale mantissa (1 + j/8); a power-of-two factor on x or s scales every
+    step exactly, so this covers all normal operands.  FMAs are emulated in
+    float64: the residual x - q0*s is exact there (checked), and the final
+    sum is rounded to fp32 once unless it lands on an fp32 midpoint (checked
+    to be absent)."""
+    x = (np.arange(1 << 23, dtype=np.uint32) | np.uint32(0x3F800000)).view(np.float32)
+    for j in range(8):
+        s = np.float32(1 + j / 8)
+        r = np.float32(1) / s
+        q0 = x * r
+        rho64 = x.astype(np.float64) - q0.astype(np.float64) * np.float64(s)
+        rho = rho64.astype(np.float32)
+        assert np.array_equal(rho.astype(np.float64), rho64)
+        s64 = q0.astype(np.float64) + rho.astype(np.float64) * np.float64(r)
+        q1 = s64.astype(np.float32)
+        up = np.nextafter(q1, np.float32(np.inf)).astype(np.float64)
+        dn = np.nextafter(q1, np.float32(-np.inf)).astype(np.float64)
+        q1d = q1.astype(np.float64)
+        assert not np.any((s64 == (q1d + up) / 2) | (s64 == (q1d + dn) / 2))
+        assert np.array_equal(q1.view(np.uint32), (x / s).view(np.uint32)), f"scale mantissa {s}"

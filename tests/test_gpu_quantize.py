@@ -49,6 +49,51 @@ def test_quantize_bit_exact(rows, k, l, scale):
     assert np.array_equal(mem, O.permuted_sf(sf.view(torch.uint8).cpu().numpy()))
 
 
+def _special_rows(k, rng):
+    """Blocks that stress the division-free quotient: values exactly at the
+    e2m1 rounding thresholds times the block scale (ties) and their fp32
+    neighbours, for scales of every e4m3 mantissa over a range of exponents;
+    -0, subnormal and tiny values beside normal ones; +-inf (IEEE-division
+    fallback); saturating scales."""
+    thr = np.array([0.25, 0.75, 1.25, 1.75, 2.5, 3.5, 5.0], np.float32)
+    rows = []
+    for mant in range(8):
+        for exp in (-9, -4, 0, 3, 8):
+            s = np.float32((1 + mant / 8) * 2.0 ** exp)
+            amax = np.float32(s * 6)                 # e4m3(amax / 6) == s exactly
+            blk = np.zeros(16, np.float32)
+            blk[0] = amax
+            t = thr * s
+            pick = rng.choice(7, 5)
+            blk[1:6] = t[pick]
+            blk[6:11] = np.nextafter(t[pick], np.float32(np.inf))
+            blk[11:15] = -np.nextafter(t[pick[:4]], np.float32(0))
+            blk[15] = -0.0
+            rows.append(blk)
+    special = np.zeros(16, np.float32)
+    special[:6] = [np.inf, -1.0, -0.0, 1e-40, -1e-40, 3.0e38]
+    rows.append(special)
+    rows.append(np.array([-0.0] * 8 + [1e-30] * 8, np.float32))
+    rows.append(np.array([-np.inf] + [0.5] * 15, np.float32))
+    rows.append(np.array([3.0e38, -2.9e38] + [1.0] * 14, np.float32))
+    flat = np.concatenate(rows)
+    n = -(-flat.size // k) * k
+    flat = np.concatenate([flat, np.zeros(n - flat.size, np.float32)])
+    return flat.reshape(-1, k)
+
+
+@pytest.mark.parametrize("k", [64, 256])
+def test_quantize_special_values_bit_exact(k):
+    rng = np.random.default_rng(k)
+    x = _special_rows(k, rng)
+    wide = (rng.standard_normal((64, k)) * np.exp2(rng.integers(-30, 30, (64, 1)))).astype(np.float32)
+    x = np.concatenate([x, wide])
+    packed, sf, _ = quantize(torch.from_numpy(x).cuda())
+    po, so = O.quantize_nvfp4(x)
+    assert np.array_equal(sf.view(torch.uint8)[:, :, 0].cpu().numpy(), so)
+    assert np.array_equal(packed.view(torch.uint8)[:, :, 0].cpu().numpy(), po)
+
+
 def test_quantize_feeds_dual_gemm():
     m, n, k = 256, 384, 1024
     g = torch.Generator().manual_seed(11)
