@@ -111,24 +111,25 @@ def quant_workload(rank, world, device):
     return xs, 0.0, nbytes, desc
 
 
-def moe_workload(rank, world, device):
+def moe_workload(rank, world, device, tokens=32768):
     """Configuration 6: MoE dispatch of configuration 4's routing (32768 tokens,
     Zipf over 64 experts, top-1) at its K = 7168: fp32 tokens -> per-expert
     NVFP4 A operands + scale atoms + permutation; HBM-bound."""
     from nvfp4_b200 import inputs as I
     from nvfp4_b200 import moe
     spec = I.GROUP_CONFIGS[4]
-    tokens, k, experts = 32768, spec["k"], 64
+    k, experts = spec["k"], 64
     g = torch.Generator().manual_seed(4000 + rank)
     x = torch.randn(tokens, k, generator=g).to(device)
-    ids = I.config4_expert_ids(seed=4 + rank).to(device)
+    ids = I.config4_expert_ids(seed=4 + rank, tokens=tokens).to(device)
     d = moe.dispatch(x, ids, experts)                  # buffers allocated once, reused per step
     torch.cuda.synchronize()
     blocks = int(d.atom_offsets[-1].item())
     rows = int(d.row_offsets[-1].item())
     nbytes = (tokens * k * 4 + tokens * 4 + rows * k // 2 + blocks * (k // 64) * 512
               + 2 * rows * 4 + 3 * (experts + 1) * 4)
-    desc = dict(workload="moe_dispatch_cfg4", tokens=tokens, k=k, experts=experts, topk=1)
+    desc = dict(workload="moe_dispatch_cfg4" if tokens == 32768 else f"moe_dispatch_{tokens}x{k}",
+                tokens=tokens, k=k, experts=experts, topk=1)
     return (x, ids, experts, d), 0.0, nbytes, desc
 
 
@@ -152,11 +153,11 @@ def shape_workload(args, device):
         dict(workload=f"grouped_gemm_{'+'.join(map(str, ms))}x{n}x{k}", groups=ms, n=n, k=k)
 
 
-def make_workload(cfg, rank, world, device):
+def make_workload(cfg, rank, world, device, tokens=32768):
     if cfg == 5:
         return quant_workload(rank, world, device)
     if cfg == 6:
-        return moe_workload(rank, world, device)
+        return moe_workload(rank, world, device, tokens)
     return dual_workload(cfg, rank, world, device) if cfg in (0, 1, 2) else \
         group_workload(cfg, rank, world, device)
 
@@ -497,6 +498,8 @@ def main():
                     help="task: the reference's own task.yml benchmark shapes, one line per task")
     ap.add_argument("--shape", default=None,
                     help="M,N,K: kernel-only dual GEMM at this size (profiling runs)")
+    ap.add_argument("--tokens", type=int, default=32768,
+                    help="configuration 6: tokens to dispatch (32768 = configuration 4's routing)")
     ap.add_argument("--group-shape", default=None,
                     help="M1:M2:...,N,K: kernel-only grouped GEMM at these sizes (profiling runs)")
     args = ap.parse_args()
@@ -527,7 +530,7 @@ def main():
     if args.shape or args.group_shape:
         cfg, data, flop, nbytes, desc = shape_workload(args, device)
     else:
-        data, flop, nbytes, desc = make_workload(cfg, rank, world, device)
+        data, flop, nbytes, desc = make_workload(cfg, rank, world, device, args.tokens)
     stream = torch.cuda.current_stream(device)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
 

@@ -727,7 +727,7 @@ extern "C" int nvfp4_moe_dispatch(const float* x, const int* expert_ids, int tok
   if (chunk_ctas > 0) {
     moe_scatter_kernel<<<chunk_ctas, 32 * kMoeWarps, hist_bytes, stream>>>(p);
     if ((rc = check_launch("moe_scatter_kernel"))) return rc;
-    const dim3 grid(p.k_atoms, (unsigned)max_blocks, 1);
+    const dim3 grid((p.k_atoms + kMoeAtomsPerCta - 1) / kMoeAtomsPerCta, (unsigned)max_blocks, 1);
     moe_quantize_kernel<<<grid, kQuantThreads, 0, stream>>>(p);
     if ((rc = check_launch("moe_quantize_kernel"))) return rc;
   }

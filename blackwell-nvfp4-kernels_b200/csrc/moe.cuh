@@ -29,7 +29,7 @@
 //               lanes with the same expert find each other with match.any,
 //               take consecutive rows after the expert's running count
 //               (stable: lower lanes and earlier steps first)
-//   4. quantise: one CTA per (128-row block of an expert, 64-deep K atom),
+//   4. quantise: one CTA per (128-row block of an expert, up to 4 64-deep K atoms),
 //               gathering its rows' tokens; grid sized by the upper bound
 //               ceil(pairs/128) + min(E, pairs) blocks, the excess exits
 //
@@ -47,6 +47,10 @@ namespace nvfp4 {
 constexpr int kMoeChunk = 1024;          // pairs per warp chunk (32 steps of 32)
 constexpr int kMoeMaxExperts = 1024;     // shared-memory histogram / scan bound
 constexpr int kMoeWarps = 4;             // chunks per CTA in count / scatter
+// K atoms per quantise CTA: the expert lookup, scale tables and row indices
+// of a CTA are shared by four atoms, and each row's 128-byte packed line is
+// written by one CTA back to back (measured 290 -> 250 us on 32768 x 7168).
+constexpr int kMoeAtomsPerCta = 4;
 
 struct MoeParams {
   const float* x;        // [T][K]
@@ -71,10 +75,15 @@ __global__ void __launch_bounds__(32 * kMoeWarps) moe_count_kernel(const MoePara
   const int chunk = blockIdx.x * kMoeWarps + warp;
   if (chunk >= p.chunks) return;
   const int p0 = chunk * kMoeChunk, p1 = min(p0 + kMoeChunk, p.pairs);
-  for (int i = p0 + lane; i < p1; i += 32) {
-    const int e = __ldg(p.ids + i);
-    if (e >= 0 && e < p.experts) atomicAdd(h + e, 1);
+  int ids[kMoeChunk / 32];                            // every load in flight before the first use
+  #pragma unroll
+  for (int s = 0; s < kMoeChunk / 32; ++s) {
+    const int i = p0 + 32 * s + lane;
+    ids[s] = i < p1 ? __ldg(p.ids + i) : -1;
   }
+  #pragma unroll
+  for (int s = 0; s < kMoeChunk / 32; ++s)
+    if (ids[s] >= 0 && ids[s] < p.experts) atomicAdd(h + ids[s], 1);
   __syncwarp();
   int* out = p.chunk_counts + (size_t)chunk * p.experts;
   for (int e = lane; e < p.experts; e += 32) out[e] = h[e];
@@ -150,15 +159,22 @@ __global__ void __launch_bounds__(32 * kMoeWarps) moe_scatter_kernel(const MoePa
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int chunk = blockIdx.x * kMoeWarps + warp;
   if (chunk >= p.chunks) return;                      // whole warps only: no block barrier below
+  const int p0 = chunk * kMoeChunk, p1 = min(p0 + kMoeChunk, p.pairs);
+  const uint32_t lt = (1u << lane) - 1u;
+  int ids[kMoeChunk / 32];                            // every load in flight before the walk
+  #pragma unroll
+  for (int s = 0; s < kMoeChunk / 32; ++s) {
+    const int i = p0 + 32 * s + lane;
+    ids[s] = i < p1 ? __ldg(p.ids + i) : -1;
+  }
   int* nr = next_row + warp * p.experts;
   const int* base = p.chunk_counts + (size_t)chunk * p.experts;
   for (int e = lane; e < p.experts; e += 32) nr[e] = p.row_offsets[e] + base[e];
   __syncwarp();
-  const int p0 = chunk * kMoeChunk, p1 = min(p0 + kMoeChunk, p.pairs);
-  const uint32_t lt = (1u << lane) - 1u;
-  for (int i0 = p0; i0 < p1; i0 += 32) {
-    const int i = i0 + lane;
-    const int e = i < p1 ? __ldg(p.ids + i) : -1;
+  #pragma unroll
+  for (int s = 0; s < kMoeChunk / 32; ++s) {
+    const int i = p0 + 32 * s + lane;
+    const int e = ids[s];
     const bool valid = e >= 0 && e < p.experts;
     const int key = valid ? e : -1;
     const uint32_t same = __match_any_sync(0xffffffffu, key);
@@ -174,12 +190,13 @@ __global__ void __launch_bounds__(32 * kMoeWarps) moe_scatter_kernel(const MoePa
   }
 }
 
-__global__ void __launch_bounds__(kQuantThreads) moe_quantize_kernel(const MoeParams p) {
-  const int atom = blockIdx.x;
+__global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) moe_quantize_kernel(const MoeParams p) {
   const int gb = blockIdx.y;                          // 128-row block over all experts
   // the expert owning block gb (atom_offsets[e] <= gb < atom_offsets[e + 1]):
   // every thread tests a few experts, one dependent load instead of a search
   __shared__ int s_expert;
+  __shared__ ScaleTables tab;
+  fill_scale_tables(tab);
   if (threadIdx.x == 0) s_expert = -1;
   __syncthreads();
   for (int i = threadIdx.x; i < p.experts; i += blockDim.x)
@@ -190,15 +207,19 @@ __global__ void __launch_bounds__(kQuantThreads) moe_quantize_kernel(const MoePa
   const int local_block = gb - p.atom_offsets[e];
   const int row0 = p.row_offsets[e] + local_block * 128;
   const int valid_rows = min(128, p.row_offsets[e + 1] - row0);
-  uint8_t* atom_base = p.sf_perm + ((size_t)gb * p.k_atoms + atom) * 512;
   const int topk = p.topk;
-  quantize_atom_block(
-      atom, atom_base,
-      [&](int r) -> const float* {
-        return r < valid_rows ? p.x + (size_t)(__ldg(p.src + row0 + r) / topk) * p.k : nullptr;
-      },
-      [&](int r) -> uint8_t* { return p.packed + (size_t)(row0 + r) * (p.k / 2); },
-      [&](int) -> uint8_t* { return nullptr; });
+  const int a1 = min(p.k_atoms, (int)(blockIdx.x + 1) * kMoeAtomsPerCta);
+  #pragma unroll 1
+  for (int atom = blockIdx.x * kMoeAtomsPerCta; atom < a1; ++atom) {   // not unrolled: measured faster
+    uint8_t* atom_base = p.sf_perm + ((size_t)gb * p.k_atoms + atom) * 512;
+    quantize_atom_block(
+        tab, atom, atom_base,
+        [&](int r) -> const float* {
+          return r < valid_rows ? p.x + (size_t)(__ldg(p.src + row0 + r) / topk) * p.k : nullptr;
+        },
+        [&](int r) -> uint8_t* { return p.packed + (size_t)(row0 + r) * (p.k / 2); },
+        [&](int) -> uint8_t* { return nullptr; });
+  }
 }
 
 struct MoeCombineParams {

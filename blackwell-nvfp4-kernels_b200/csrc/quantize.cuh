@@ -17,10 +17,12 @@
 // equals RN(x / s) for every fp32 x and every e4m3 scale s (s has one of 8
 // mantissas; scaling x or s by a power of two scales every step exactly, so
 // the exhaustive check over all 2^23 mantissas of x times the 8 mantissas of
-// s covers all normal operands; tests/test_formats.py repeats it).  Two
-// inputs need care: x = -0 (the FMA sum gives +0: the sign is copied back
-// from x) and x = +-inf (the residual is NaN: a block whose amax is infinite
-// uses IEEE division).  Tiny quotients only need their sign to be right.
+// s covers all normal operands; tests/test_formats.py repeats it).  The
+// residual is exact whenever it is nonzero, so it is computed rounding down:
+// an exact zero then comes out as -0, which leaves q0 unchanged and gives
+// x = +-0 the quotient +-0 that IEEE division gives.  x = +-inf makes the
+// residual NaN: a block whose amax is infinite uses IEEE division.  The
+// same two FMAs divide amax by 6 (mantissa 1.5, one of the 8 checked).
 //   scale == 0 -> all values 0.
 //
 // HBM-bound: 4 bytes read and 0.5625 (+0.0625 plain scales) written per element.
@@ -59,6 +61,33 @@ __device__ __forceinline__ uint32_t e2m1x2(float lo, float hi) {
 // 4 packed bytes, and the row's four scale bytes are gathered into one
 // 4-byte word of the scale atom (byte (r%32)*16 + ((r/32)%4)*4 + block).
 constexpr int kQuantThreads = 256;
+// Resident CTAs per SM the quantise kernels are compiled for (a 64-register
+// cap): the kernels are latency-bound on their loads, and four CTAs per SM
+// measured best (three: 6% slower; five or six: spills, slower).
+constexpr int kQuantCtasPerSm = 4;
+
+// RN(x / s) for s one of the e4m3 values (or 6) and r = RN(1/s).
+__device__ __forceinline__ float div_by_scale(float x, float s, float r) {
+  const float q0 = __fmul_rn(x, r);
+  return __fmaf_rn(__fmaf_rd(-q0, s, x), r, q0);
+}
+
+// Per-CTA tables over the 128 non-negative e4m3 codes: the scale's value and
+// RN(1/value) (0 for code 0), one shared-memory load each instead of two
+// conversions and an IEEE reciprocal per 8 values.
+struct ScaleTables {
+  float val[128];
+  float rcp[128];
+};
+
+// Every thread of the CTA must call this, then __syncthreads() before use.
+__device__ __forceinline__ void fill_scale_tables(ScaleTables& t) {
+  for (int c = threadIdx.x; c < 128; c += blockDim.x) {
+    const float v = __half2float(__half(__nv_cvt_fp8_to_halfraw((__nv_fp8_storage_t)c, __NV_E4M3)));
+    t.val[c] = v;
+    t.rcp[c] = v == 0.f ? 0.f : __frcp_rn(v);
+  }
+}
 
 // The body shared by the plain quantiser and the MoE gather-quantiser: rows
 // r = 0..127 of one 128-row block, one 64-deep K atom.  src(r) -> the fp32
@@ -66,8 +95,9 @@ constexpr int kQuantThreads = 256;
 // plain(r) -> the plain-scale row or nullptr; atom_base -> the block's
 // 512-byte scale atom for this K atom (padding rows get zero scales).
 template <class Src, class Packed, class Plain>
-__device__ __forceinline__ void quantize_atom_block(int atom, uint8_t* atom_base, Src src,
-                                                    Packed packed, Plain plain) {
+__device__ __forceinline__ void quantize_atom_block(const ScaleTables& tab, int atom,
+                                                    uint8_t* atom_base, Src src, Packed packed,
+                                                    Plain plain) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int sub = lane & 7;                    // which 8 values of the 64-value row segment
   constexpr int kSteps = 128 / (4 * (kQuantThreads / 32));
@@ -96,21 +126,18 @@ __device__ __forceinline__ void quantize_atom_block(int atom, uint8_t* atom_base
     #pragma unroll
     for (int e = 0; e < 8; ++e) amax = fmaxf(amax, fabsf(v[step][e]));
     amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, 1));   // the block's other half
-    const __nv_fp8_storage_t s8 =
-        __nv_cvt_float_to_fp8(__fdiv_rn(amax, 6.0f), __NV_SATFINITE, __NV_E4M3);
-    const float s = __half2float(__half(__nv_cvt_fp8_to_halfraw(s8, __NV_E4M3)));
+    const bool finite = amax <= 3.402823466e38f;
+    const float a6 = finite ? div_by_scale(amax, 6.0f, 1.0f / 6.0f) : amax;
+    const __nv_fp8_storage_t s8 = __nv_cvt_float_to_fp8(a6, __NV_SATFINITE, __NV_E4M3);
+    const float s = tab.val[s8];
     float q[8];
     if (s == 0.f) {
       #pragma unroll
       for (int e = 0; e < 8; ++e) q[e] = 0.f;
-    } else if (amax <= 3.402823466e38f) {
-      const float rs = __frcp_rn(s);
+    } else if (finite) {
+      const float rs = tab.rcp[s8];
       #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float x = v[step][e];
-        const float q0 = __fmul_rn(x, rs);
-        q[e] = copysignf(__fmaf_rn(__fmaf_rn(-q0, s, x), rs, q0), x);
-      }
+      for (int e = 0; e < 8; ++e) q[e] = div_by_scale(v[step][e], s, rs);
     } else {                                   // an infinite value in the block
       #pragma unroll
       for (int e = 0; e < 8; ++e) q[e] = __fdiv_rn(v[step][e], s);
@@ -118,12 +145,10 @@ __device__ __forceinline__ void quantize_atom_block(int atom, uint8_t* atom_base
     uint32_t word = 0;
     #pragma unroll
     for (int e = 0; e < 4; ++e) word |= e2m1x2(q[2 * e], q[2 * e + 1]) << (8 * e);
-    // scale bytes of blocks 0..3 of this row sit in lanes sub = 0, 2, 4, 6
-    const int row_lane0 = lane & ~7;
-    uint32_t sf_word = 0;
-    #pragma unroll
-    for (int b = 0; b < 4; ++b)
-      sf_word |= (__shfl_sync(0xffffffffu, (uint32_t)s8, row_lane0 + 2 * b) & 0xffu) << (8 * b);
+    // scale bytes of blocks 0..3 of this row sit in lanes sub = 0, 2, 4, 6:
+    // pairs first (sub 0: blocks 0,1; sub 4: blocks 2,3), then the halves
+    const uint32_t pair = (uint32_t)s8 | (__shfl_down_sync(0xffffffffu, (uint32_t)s8, 2) << 8);
+    const uint32_t sf_word = pair | (__shfl_down_sync(0xffffffffu, pair, 4) << 16);   // sub 0
     if (valid) {
       *reinterpret_cast<uint32_t*>(packed(r) + (size_t)atom * 32 + 4 * sub) = word;
       uint8_t* pl = plain(r);
@@ -135,7 +160,12 @@ __device__ __forceinline__ void quantize_atom_block(int atom, uint8_t* atom_base
   }
 }
 
-__global__ void __launch_bounds__(kQuantThreads) quantize_nvfp4_kernel(const QuantParams p) {
+// One K atom per CTA (measured: several atoms per CTA, as the MoE quantiser
+// uses, leave too few CTAs for the last wave on operand-sized inputs).
+__global__ void __launch_bounds__(kQuantThreads, kQuantCtasPerSm) quantize_nvfp4_kernel(const QuantParams p) {
+  __shared__ ScaleTables tab;
+  fill_scale_tables(tab);
+  __syncthreads();
   const int atom = blockIdx.x;                 // k-atom index (64 K per atom)
   const int rb = blockIdx.y;                   // 128-row block
   const int l = blockIdx.z;
@@ -143,7 +173,7 @@ __global__ void __launch_bounds__(kQuantThreads) quantize_nvfp4_kernel(const Qua
   const size_t row0 = (size_t)l * p.rows + (size_t)rb * 128;
   const int valid_rows = min(128, p.rows - rb * 128);
   quantize_atom_block(
-      atom, atom_base,
+      tab, atom, atom_base,
       [&](int r) -> const float* { return r < valid_rows ? p.x + (row0 + r) * (size_t)p.k : nullptr; },
       [&](int r) -> uint8_t* { return p.packed + (row0 + r) * (size_t)(p.k / 2); },
       [&](int r) -> uint8_t* { return p.sf_plain ? p.sf_plain + (row0 + r) * (size_t)(p.k / 16) : nullptr; });

@@ -113,7 +113,9 @@ def test_dual_config0_quantisation_matches_oracle():
 
 def test_reciprocal_fma_quotient_is_ieee_division():
     """The device quantiser forms x / s without a division: r = RN(1/s),
-    q0 = RN(x*r), q1 = RN(q0 + RN(x - q0*s) * r) (two FMAs).  Exhaustive
+    q0 = RN(x*r), q1 = RN(q0 + RD(x - q0*s) * r) (two FMAs; the residual is
+    exact whenever it is nonzero, asserted below, so its rounding direction
+    only decides the sign of a zero residual, which leaves q0 unchanged).  Exhaustive
     check that q1 == RN(x/s) for every fp32 mantissa of x and every e4m3
     scale mantissa (1 + j/8); a power-of-two factor on x or s scales every
     step exactly, so this covers all normal operands.  FMAs are emulated in
