@@ -102,6 +102,7 @@ struct Knobs {
   bool dual_pair = false;  // NVFP4_DUAL_KERNEL=pair: the CTA-pair kernel
   int dual_cluster = 0;    // NVFP4_DUAL_CLUSTER: 0 automatic, 1 off, 2 / 4 forced cluster split-K
   int grouped_bn = 0;      // NVFP4_GROUPED_BN (128 / 256; 0 = automatic)
+  bool pdl = true;         // NVFP4_PDL=0: launch the GEMMs without programmatic dependent launch
 };
 
 Knobs read_knobs() {
@@ -121,6 +122,7 @@ Knobs read_knobs() {
     else if ((x = val("DUAL_KERNEL"))) k.dual_pair = strcmp(x, "pair") == 0;
     else if ((x = val("DUAL_CLUSTER"))) k.dual_cluster = atoi(x);
     else if ((x = val("GROUPED_BN"))) k.grouped_bn = atoi(x);
+    else if ((x = val("PDL"))) k.pdl = atoi(x) != 0;
   }
   if (k.dual_group_m < 1) k.dual_group_m = 1;
   return k;
@@ -296,6 +298,45 @@ int choose_splits(int tiles, int k_blocks, int num_sms) {
   return s < 1 ? 1 : s;
 }
 
+// Programmatic dependent launch for the GEMM kernels on this thread's calls
+// (set from the knobs at every entry point).  The kernels build their
+// barriers and TMEM allocation while the previous kernel in the stream is
+// still running and wait on griddepcontrol before touching global memory;
+// each kernel is persistent (every CTA resident from the start), so letting
+// the next one be scheduled early cannot starve it of SMs.
+thread_local bool t_pdl = true;
+
+// cudaLaunchKernelEx with programmatic stream serialization (when enabled)
+// and an optional cluster dimension.
+template <class Kern, class Params>
+int launch_gemm(Kern kern, unsigned grid, int threads, int smem, cudaStream_t stream,
+                const Params& p, int cluster, const char* what) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3((unsigned)threads, 1, 1);
+  cfg.dynamicSmemBytes = (size_t)smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  unsigned n = 0;
+  if (cluster > 0) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = (unsigned)cluster;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (t_pdl) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
+  if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+  return check_launch(what);
+}
+
 // ---------------------------------------------------------------- dual GEMM
 // Cluster split-K launch: grid = tiles * S CTAs in clusters of S (one unit
 // per CTA), no workspace.
@@ -306,22 +347,8 @@ int launch_dual_cluster(DeviceState* d, int slot, DualParams& p, cudaStream_t st
   int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
   if (rc) return rc;
   p.splits = S;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)(p.tiles * S), 1, 1);
-  cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
-  cfg.dynamicSmemBytes = Cfg::kSmemBytes;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = S;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, p);
-  if (e != cudaSuccess)
-    return fail(NVFP4_ERR_CUDA, "dual_gemm_kernel (cluster %d) launch: %s", S, cudaGetErrorString(e));
-  return check_launch("dual_gemm_kernel (cluster split-K)");
+  return launch_gemm(kern, (unsigned)(p.tiles * S), Cfg::kThreads, Cfg::kSmemBytes, stream, p, S,
+                     "dual_gemm_kernel (cluster split-K)");
 }
 
 // How many S-CTA clusters of the cluster split-K kernel fit on the device at
@@ -395,13 +422,13 @@ int launch_dual(DeviceState* d, int slot, DualParams& p, int forced_splits, int 
   if (p.splits > 1) {
     auto kern = dual_gemm_kernel<kBN, kStages, kEpiWarps, kAccBufs, true>;
     if ((rc = set_smem_once(d, slot + 10, kern, Cfg::kSmemBytes))) return rc;
-    kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
-  } else {
-    auto kern = dual_gemm_kernel<kBN, kStages, kEpiWarps, kAccBufs, false>;
-    if ((rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes))) return rc;
-    kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
+    return launch_gemm(kern, (unsigned)grid, Cfg::kThreads, Cfg::kSmemBytes, stream, p, 0,
+                       "dual_gemm_kernel (split-K)");
   }
-  return check_launch("dual_gemm_kernel");
+  auto kern = dual_gemm_kernel<kBN, kStages, kEpiWarps, kAccBufs, false>;
+  if ((rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes))) return rc;
+  return launch_gemm(kern, (unsigned)grid, Cfg::kThreads, Cfg::kSmemBytes, stream, p, 0,
+                     "dual_gemm_kernel");
 }
 
 // CTA-pair kernel with 96-column tiles, 192-wide MMAs and two accumulator buffers.
@@ -434,8 +461,8 @@ int launch_dual_2sm(DeviceState* d, int slot, const void* a, const void* b1, con
   if ((rc = encode_operand(&p.tmap_b1, b1, n, k, l, Cfg::kBN))) return rc;
   if ((rc = encode_operand(&p.tmap_b2, b2, n, k, l, Cfg::kBN))) return rc;
   const int pairs = p.tiles < d->num_sms / 2 ? p.tiles : d->num_sms / 2;
-  kern<<<2 * pairs, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
-  return check_launch("dual_gemm_2sm_kernel");
+  return launch_gemm(kern, (unsigned)(2 * pairs), Cfg::kThreads, Cfg::kSmemBytes, stream, p, 0,
+                     "dual_gemm_2sm_kernel");
 }
 
 // ---------------------------------------------------------------- grouped GEMM
@@ -468,8 +495,8 @@ int launch_grouped_chunk(DeviceState* d, int slot, const nvfp4_group* gs, const 
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
   const int grid = tiles < d->num_sms ? tiles : d->num_sms;
-  kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
-  return check_launch("grouped_gemm_kernel");
+  return launch_gemm(kern, (unsigned)grid, Cfg::kThreads, Cfg::kSmemBytes, stream, p, 0,
+                     "grouped_gemm_kernel");
 }
 
 // 128x256 tiles (4 stages, 8 epilogue warps, one accumulator buffer) when
@@ -518,6 +545,7 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   p.m_blocks = (m + kBM - 1) / kBM;
   p.k_blocks = k / kBK;
   const Knobs kn = read_knobs();
+  t_pdl = kn.pdl;
   p.group_m = kn.dual_group_m;
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
@@ -577,7 +605,9 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
   int min_n = groups[live[0]].n;
   for (int i : live) min_n = groups[i].n < min_n ? groups[i].n : min_n;
   int bn = min_n >= 256 ? 256 : 128;
-  const int forced = read_knobs().grouped_bn;
+  const Knobs kn = read_knobs();
+  t_pdl = kn.pdl;
+  const int forced = kn.grouped_bn;
   if (forced == 128 || forced == 256) bn = forced;
   if (n <= 16) return launch_grouped<16>(d, groups, live.data(), n, bn, stream);
   for (int s = 0; s < n; s += 96) {

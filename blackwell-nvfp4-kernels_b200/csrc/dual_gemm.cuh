@@ -189,6 +189,10 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
   tc_fence_after();
   const uint32_t tmem = s_tmem_base;
   const AbortCtl ctl{&s_abort, p.status, p.wait_limit};
+  // everything above (barriers, TMEM, descriptor prefetch) overlaps the
+  // previous kernel in the stream; global memory only after it completed
+  griddep_wait();
+  if (threadIdx.x == 0) griddep_launch_dependents();
 
   if (warp == kEpiWarps) {
     // ------------------------------------------------------------ TMA producer

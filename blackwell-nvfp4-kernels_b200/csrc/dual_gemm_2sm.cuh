@@ -146,6 +146,9 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
   cluster_sync();   // the peer's barriers exist before anyone signals them
   tc_fence_after();
   const uint32_t tmem = s_tmem_base;
+  // the prologue above overlaps the previous kernel; global memory only after it
+  griddep_wait();
+  if (threadIdx.x == 0) griddep_launch_dependents();
   const AbortCtl ctl{&s_abort, p.status, p.wait_limit};
   const int rest_k = p.k / kKStep;   // 64-deep atoms per 128-row block
 

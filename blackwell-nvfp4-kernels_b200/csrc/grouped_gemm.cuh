@@ -128,6 +128,9 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem_base;
+  // the prologue above overlaps the previous kernel; global memory only after it
+  griddep_wait();
+  if (threadIdx.x == 0) griddep_launch_dependents();
   const AbortCtl ctl{&s_abort, p.status, p.wait_limit};
 
   if (warp == kProd) {
