@@ -99,7 +99,7 @@ struct Knobs {
   int dual_group_m = 32;   // NVFP4_DUAL_GROUP_M (measured: 16 -> 32 saves ~1.5% on 8192x14336x4096)
   int dual_splits = 0;     // NVFP4_DUAL_SPLITS (0 = automatic)
   int dual_bn = 0;         // NVFP4_DUAL_BN (64 / 128, or 96 / 128 for the pair kernel; 0 = automatic)
-  bool dual_pair = false;  // NVFP4_DUAL_KERNEL=pair: the CTA-pair kernel
+  int dual_kernel = 0;     // NVFP4_DUAL_KERNEL: 0 automatic, 1 pair (CTA-pair kernel), 2 single
   int dual_cluster = 0;    // NVFP4_DUAL_CLUSTER: 0 automatic, 1 off, 2 / 4 forced cluster split-K
   int grouped_bn = 0;      // NVFP4_GROUPED_BN (128 / 256; 0 = automatic)
   bool pdl = true;         // NVFP4_PDL=0: launch the GEMMs without programmatic dependent launch
@@ -119,7 +119,8 @@ Knobs read_knobs() {
     if ((x = val("DUAL_GROUP_M"))) k.dual_group_m = atoi(x);
     else if ((x = val("DUAL_SPLITS"))) k.dual_splits = atoi(x);
     else if ((x = val("DUAL_BN"))) k.dual_bn = atoi(x);
-    else if ((x = val("DUAL_KERNEL"))) k.dual_pair = strcmp(x, "pair") == 0;
+    else if ((x = val("DUAL_KERNEL")))
+      k.dual_kernel = strcmp(x, "pair") == 0 ? 1 : strcmp(x, "single") == 0 ? 2 : 0;
     else if ((x = val("DUAL_CLUSTER"))) k.dual_cluster = atoi(x);
     else if ((x = val("GROUPED_BN"))) k.grouped_bn = atoi(x);
     else if ((x = val("PDL"))) k.pdl = atoi(x) != 0;
@@ -551,13 +552,25 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   p.wait_limit = wait_limit_cycles();
 
   // Kernel choice: the single-CTA kernel (128-wide tiles; cluster split-K
-  // when the tiles leave SMs idle; 64-wide tiles on request).  The CTA-pair
-  // kernel (NVFP4_DUAL_KERNEL=pair; 96-wide tiles with NVFP4_DUAL_BN=96)
-  // loads a third fewer operand bytes per SM and issues half the MMA
-  // instructions, but measures ~8% slower on configuration 1 (478 vs 443 us;
-  // 96-wide: 618 us): the pair's two-CTA handshakes on every stage cost more
-  // than the bytes save.
-  if (kn.dual_pair) {
+  // when the tiles leave SMs idle; 64-wide tiles on request), or the CTA-pair
+  // kernel (NVFP4_DUAL_KERNEL=pair; 96-wide tiles with NVFP4_DUAL_BN=96),
+  // which loads a third fewer operand bytes per SM but measures ~3% slower
+  // on configuration 1 (440 vs 428 us).  Automatic choice of the pair: one
+  // pair block per batch (128 < M <= 256: both SMs of a pair hold real rows
+  // and B is fetched once instead of once per 128-row block), the
+  // single-CTA kernel would split K, at least 48 CTAs, at most 32 K blocks
+  // (longer K favours the split).  Measured (us, single vs pair):
+  // 256x3072x4096 24.5 / 21.9, 256x4096x7168 30.3 / 28.4, 200x4096x7168
+  // 30.2 / 29.0, 256x7168x2048 19.7 / 19.9; kept single: 256x2048x7168
+  // 26.4 / 27.4, 256x1024x16384 28.3 / 42.1.
+  bool pair = kn.dual_kernel == 1;
+  if (kn.dual_kernel == 0 && kn.dual_bn == 0 && kn.dual_splits == 0 && kn.dual_cluster == 0 &&
+      m > 128 && m <= 256) {
+    const int single_tiles = l * ((m + kBM - 1) / kBM) * ((n + 127) / 128);
+    const int pair_ctas = 2 * l * ((n + 127) / 128);
+    pair = single_tiles < d->num_sms && pair_ctas >= 48 && pair_ctas <= d->num_sms && p.k_blocks <= 32;
+  }
+  if (pair) {
     if (kn.dual_bn == 96)
       return launch_dual_2sm<96, 5>(d, 3, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
                                     kn.dual_group_m, stream);

@@ -169,7 +169,11 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
         const int blk0 = n0 / 128;
         const int blk1 = min(blk0 + 1, p.sfb_blocks - 1);   // past N: re-read the last block
         const size_t atoms = (size_t)rest_k * kSfAtom;
-        const uint8_t* sfa_t = p.sfa + ((size_t)tc.l * p.sfa_blocks + m0 / 128) * atoms;
+        // the second CTA of the last pair block may lie wholly past M (odd
+        // ceil(M/128)): its A rows load as zeros, it stores nothing, and it
+        // re-reads the last real scale block rather than reading past the tensor
+        const int ablk = min(m0 / 128, p.sfa_blocks - 1);
+        const uint8_t* sfa_t = p.sfa + ((size_t)tc.l * p.sfa_blocks + ablk) * atoms;
         const uint8_t* sfb1_0 = p.sfb1 + ((size_t)tc.l * p.sfb_blocks + blk0) * atoms;
         const uint8_t* sfb1_1 = p.sfb1 + ((size_t)tc.l * p.sfb_blocks + blk1) * atoms;
         const uint8_t* sfb2_0 = p.sfb2 + ((size_t)tc.l * p.sfb_blocks + blk0) * atoms;

@@ -84,7 +84,8 @@ def test_dual_task_shapes(m, n, k, l, kernel, monkeypatch):
 
 
 @pytest.mark.parametrize("m,n,k,l", [(256, 128, 256, 1), (384, 640, 1024, 2), (200, 264, 512, 1),
-                                     (130, 72, 768, 1), (1, 8, 256, 1), (1000, 1000, 2048, 1)])
+                                     (130, 72, 768, 1), (1, 8, 256, 1), (1000, 1000, 2048, 1),
+                                     (128, 1024, 2048, 1), (100, 256, 1024, 3)])
 @pytest.mark.parametrize("bn", ["128", "96"])
 def test_dual_pair_kernel_edges(m, n, k, l, bn, monkeypatch):
     """CTA-pair kernel (128- and 96-wide tiles): M not a multiple of 256
