@@ -471,7 +471,7 @@ template <int kBN, int kStages, int kEpiWarps, int kAccBufs, int kMaxGroups>
 int launch_grouped_chunk(DeviceState* d, int slot, const nvfp4_group* gs, const int* idx, int count,
                          cudaStream_t stream) {
   using Cfg = GroupedCfg<kBN, kStages, kEpiWarps, kAccBufs>;
-  auto kern = grouped_gemm_kernel<kBN, kStages, kEpiWarps, kAccBufs, kMaxGroups>;
+  auto kern = grouped_gemm_kernel<kBN, kStages, kEpiWarps, kAccBufs, GroupedParams<kMaxGroups>>;
   int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
   if (rc) return rc;
   static thread_local GroupedParams<kMaxGroups> p;
@@ -509,6 +509,40 @@ int launch_grouped(DeviceState* d, const nvfp4_group* gs, const int* idx, int co
   const int base = kMaxGroups == 16 ? 4 : 6;
   if (bn == 256) return launch_grouped_chunk<256, 4, 8, 1, kMaxGroups>(d, base, gs, idx, count, stream);
   return launch_grouped_chunk<128, 6, 4, 2, kMaxGroups>(d, base + 1, gs, idx, count, stream);
+}
+
+// MoE mode: up to kMoeMaxExpertsPerLaunch experts per launch, sizes read on
+// the device; the grid is persistent over the upper bound of the tiles.
+constexpr int kMoeMaxExpertsPerLaunch = 128;
+
+template <int kBN, int kStages, int kEpiWarps, int kAccBufs>
+int launch_moe_grouped_chunk(DeviceState* d, int slot, const void* a, int a_rows, const void* sfa,
+                             const int* counts, const int* row_offsets, const int* atom_offsets,
+                             const void* const* b, const void* const* sfb, int e0, int count,
+                             int n, int k, void* c, cudaStream_t stream) {
+  using Cfg = GroupedCfg<kBN, kStages, kEpiWarps, kAccBufs>;
+  using P = MoeGemmParams<kMoeMaxExpertsPerLaunch>;
+  auto kern = grouped_gemm_kernel<kBN, kStages, kEpiWarps, kAccBufs, P>;
+  int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
+  if (rc) return rc;
+  static thread_local P p;
+  if ((rc = encode_operand(&p.tmap_a, a, a_rows, k, 1, kBM))) return rc;
+  for (int i = 0; i < count; ++i) {
+    if ((rc = encode_operand(&p.tmap_b[i], b[e0 + i], n, k, 1, kBN))) return rc;
+    p.sfb[i] = static_cast<const uint8_t*>(sfb[e0 + i]);
+  }
+  p.sfa = static_cast<const uint8_t*>(sfa);
+  p.counts = counts, p.row_offsets = row_offsets, p.atom_offsets = atom_offsets;
+  p.c = static_cast<__half*>(c);
+  p.e0 = e0, p.experts = count, p.n = n, p.k = k;
+  p.lines32 = (n % 16 == 0) && (reinterpret_cast<uintptr_t>(c) % 32 == 0);
+  p.status = d->status;
+  p.wait_limit = wait_limit_cycles();
+  // tiles <= (ceil(rows / 128) + experts) * n_blocks whatever the routing
+  const long long bound = ((long long)(a_rows + kBM - 1) / kBM + count) * ((n + kBN - 1) / kBN);
+  const int grid = bound < d->num_sms ? (int)bound : d->num_sms;
+  return launch_gemm(kern, (unsigned)grid, Cfg::kThreads, Cfg::kSmemBytes, stream, p, 0,
+                     "grouped_gemm_kernel (MoE)");
 }
 
 }  // namespace
@@ -707,6 +741,51 @@ extern "C" int nvfp4_quantize(const float* x, int rows, int k, int l, void* pack
 // ---------------------------------------------------------------------------
 // MoE dispatch (route -> per-expert NVFP4 A operands) and combine.
 // ---------------------------------------------------------------------------
+extern "C" int nvfp4_moe_grouped_gemm(const void* a_packed, int a_rows, const void* sfa_atoms,
+                                      const int* counts, const int* row_offsets,
+                                      const int* atom_offsets, const void* const* b,
+                                      const void* const* sfb_perm, int num_experts, int n, int k,
+                                      void* c, void* stream_) {
+  if (a_rows < 0 || num_experts < 1 || n < 1 || k < 1)
+    return fail(NVFP4_ERR_INVALID_ARG, "bad sizes (rows=%d experts=%d n=%d k=%d)", a_rows,
+                num_experts, n, k);
+  if (k % kBK != 0) return fail(NVFP4_ERR_SHAPE, "K=%d is not a multiple of 256", k);
+  if (n % 8 != 0) return fail(NVFP4_ERR_SHAPE, "N=%d is not a multiple of 8", n);
+  if ((long long)a_rows * n >= (1LL << 40) || (long long)a_rows * k >= (1LL << 41))
+    return fail(NVFP4_ERR_SHAPE, "problem too large");
+  if (a_rows == 0) return NVFP4_OK;
+  if (!a_packed || !sfa_atoms || !counts || !row_offsets || !atom_offsets || !b || !sfb_perm || !c)
+    return fail(NVFP4_ERR_INVALID_ARG, "null pointer argument");
+  if (!aligned16(a_packed) || !aligned16(sfa_atoms) || !aligned16(c))
+    return fail(NVFP4_ERR_ALIGNMENT, "a/sfa/c must be 16-byte aligned");
+  for (int e = 0; e < num_experts; ++e) {
+    if (!b[e] || !sfb_perm[e]) return fail(NVFP4_ERR_INVALID_ARG, "expert %d: null weights", e);
+    if (!aligned16(b[e]) || !aligned16(sfb_perm[e]))
+      return fail(NVFP4_ERR_ALIGNMENT, "expert %d: weights must be 16-byte aligned", e);
+  }
+  DeviceState* d = nullptr;
+  int rc = get_device(&d);
+  if (rc) return rc;
+  const cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  const Knobs kn = read_knobs();
+  t_pdl = kn.pdl;
+  int bn = n >= 256 ? 256 : 128;
+  if (kn.grouped_bn == 128 || kn.grouped_bn == 256) bn = kn.grouped_bn;
+  for (int e0 = 0; e0 < num_experts; e0 += kMoeMaxExpertsPerLaunch) {
+    const int cnt = num_experts - e0 < kMoeMaxExpertsPerLaunch ? num_experts - e0
+                                                               : kMoeMaxExpertsPerLaunch;
+    rc = bn == 256
+             ? launch_moe_grouped_chunk<256, 4, 8, 1>(d, 22, a_packed, a_rows, sfa_atoms, counts,
+                                                      row_offsets, atom_offsets, b, sfb_perm, e0,
+                                                      cnt, n, k, c, stream)
+             : launch_moe_grouped_chunk<128, 6, 4, 2>(d, 23, a_packed, a_rows, sfa_atoms, counts,
+                                                      row_offsets, atom_offsets, b, sfb_perm, e0,
+                                                      cnt, n, k, c, stream);
+    if (rc) return rc;
+  }
+  return NVFP4_OK;
+}
+
 extern "C" size_t nvfp4_moe_workspace_bytes(int tokens, int topk, int num_experts) {
   if (tokens < 0 || topk < 1 || num_experts < 1) return 0;
   const long long pairs = (long long)tokens * topk;

@@ -69,31 +69,138 @@ struct GroupedCfg {
   static_assert(kEpiWarps % 4 == 0 && kColsPerWarp % 32 == 0, "epilogue split");
 };
 
+// MoE mode: the experts' A operands are consecutive row ranges of one packed
+// buffer (the MoE dispatch's output) and their sizes live on the device, so
+// the launch needs no host round trip.  Expert e0 + i has counts[e0 + i]
+// rows from row row_offsets[e0 + i] and its scale atoms from 128-row block
+// atom_offsets[e0 + i] of sfa; its output rows are the same rows of c.  The
+// tile schedule is built in shared memory from those arrays when the kernel
+// starts.  A tile's rows past its expert's count belong to the next expert:
+// they are computed and never stored.
+template <int kMaxExperts>
+struct MoeGemmParams {
+  CUtensorMap tmap_a;                // packed rows [rows][K/2], box {128 B, 128 rows, 1}
+  CUtensorMap tmap_b[kMaxExperts];   // expert weights [N][K/2], box {128 B, BN rows, 1}
+  const uint8_t* sfb[kMaxExperts];   // [ceil(N/128)][K/64][512]
+  const uint8_t* sfa;                // dispatch scale atoms
+  const int* counts;                 // device arrays of the dispatch, indexed e0 + i
+  const int* row_offsets;
+  const int* atom_offsets;
+  __half* c;                         // [rows][N]
+  int e0, experts, n, k, lines32;
+  unsigned* status;
+  long long wait_limit;
+};
+
 struct GTile { int g, l, mb, nb; };
 
-template <int kMaxGroups>
-__device__ __forceinline__ GTile grouped_tile(const GroupedParams<kMaxGroups>& p, int t) {
-  int lo = 0, hi = p.num_groups - 1;  // largest g with tile_start <= t
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (p.g[mid].tile_start <= t) lo = mid; else hi = mid - 1;
-  }
-  const GroupInfo& gi = p.g[lo];
-  GTile r;
-  r.g = lo;
-  int local = t - gi.tile_start;
-  const int per_l = gi.m_blocks * gi.n_blocks;
-  r.l = local / per_l;
-  local -= r.l * per_l;
-  r.mb = local % gi.m_blocks;
-  r.nb = local / gi.m_blocks;
-  return r;
-}
+// What the kernel roles need of one group.
+struct GroupView {
+  const CUtensorMap* tmap_a;
+  const CUtensorMap* tmap_b;
+  int a_row0;                        // first row of the group in tmap_a
+  const uint8_t* sfa;
+  const uint8_t* sfb;
+  __half* c;
+  int m, n, k, l, m_blocks, n_blocks, lines32;
+};
 
-template <int kBN, int kStages, int kEpiWarps, int kAccBufs, int kMaxGroups>
+// Tile schedule: the table mode reads the parameter block, the MoE mode a
+// shared-memory copy of the device sizes (filled once per CTA).
+template <class P, int kBN> struct Schedule;
+
+template <int kMaxGroups, int kBN>
+struct Schedule<GroupedParams<kMaxGroups>, kBN> {
+  struct Storage {};
+  const GroupedParams<kMaxGroups>& p;
+  __device__ Schedule(const GroupedParams<kMaxGroups>& p_, Storage&) : p(p_) {}
+  __device__ static constexpr bool needs_fill() { return false; }
+  __device__ void fill() {}
+  __device__ int tiles() const { return p.tiles; }
+  __device__ GTile tile(int t) const {
+    int lo = 0, hi = p.num_groups - 1;  // largest g with tile_start <= t
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (p.g[mid].tile_start <= t) lo = mid; else hi = mid - 1;
+    }
+    const GroupInfo& gi = p.g[lo];
+    GTile r;
+    r.g = lo;
+    int local = t - gi.tile_start;
+    const int per_l = gi.m_blocks * gi.n_blocks;
+    r.l = local / per_l;
+    local -= r.l * per_l;
+    r.mb = local % gi.m_blocks;
+    r.nb = local / gi.m_blocks;
+    return r;
+  }
+  __device__ GroupView view(int g) const {
+    const GroupInfo& gi = p.g[g];
+    return GroupView{&p.tmap_a[g], &p.tmap_b[g], 0, gi.sfa, gi.sfb, gi.c, gi.m, gi.n, gi.k, gi.l,
+                     gi.m_blocks, gi.n_blocks, gi.lines32};
+  }
+};
+
+template <int kMaxExperts, int kBN>
+struct Schedule<MoeGemmParams<kMaxExperts>, kBN> {
+  struct Storage {
+    int tile_start[kMaxExperts + 1];
+    int rows[kMaxExperts], row0[kMaxExperts], atom0[kMaxExperts];
+  };
+  const MoeGemmParams<kMaxExperts>& p;
+  Storage& s;
+  __device__ Schedule(const MoeGemmParams<kMaxExperts>& p_, Storage& s_) : p(p_), s(s_) {}
+  __device__ static constexpr bool needs_fill() { return true; }
+  // every thread calls this (after the dispatch that wrote the sizes has
+  // completed), then __syncthreads()
+  __device__ void fill() {
+    const int n_blocks = (p.n + kBN - 1) / kBN;
+    for (int i = threadIdx.x; i < p.experts; i += blockDim.x) {
+      s.rows[i] = p.counts[p.e0 + i];
+      s.row0[i] = p.row_offsets[p.e0 + i];
+      s.atom0[i] = p.atom_offsets[p.e0 + i];
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      int t = 0;
+      for (int i = 0; i < p.experts; ++i) {
+        s.tile_start[i] = t;
+        t += (s.rows[i] + kBM - 1) / kBM * n_blocks;
+      }
+      s.tile_start[p.experts] = t;
+    }
+  }
+  __device__ int tiles() const { return s.tile_start[p.experts]; }
+  __device__ GTile tile(int t) const {
+    int lo = 0, hi = p.experts - 1;     // largest i with tile_start <= t and tiles of its own
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s.tile_start[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    GTile r;
+    r.g = lo;
+    r.l = 0;
+    const int local = t - s.tile_start[lo];
+    const int m_blocks = (s.rows[lo] + kBM - 1) / kBM;
+    r.mb = local % m_blocks;
+    r.nb = local / m_blocks;
+    return r;
+  }
+  __device__ GroupView view(int i) const {
+    const int m = s.rows[i];
+    return GroupView{&p.tmap_a, &p.tmap_b[i], s.row0[i],
+                     p.sfa + (size_t)s.atom0[i] * (p.k / kKStep) * kSfAtom, p.sfb[i],
+                     p.c + (size_t)s.row0[i] * p.n, m, p.n, p.k, 1, (m + kBM - 1) / kBM,
+                     (p.n + kBN - 1) / kBN, p.lines32};
+  }
+};
+
+template <int kBN, int kStages, int kEpiWarps, int kAccBufs, class P>
 __global__ void __launch_bounds__(GroupedCfg<kBN, kStages, kEpiWarps, kAccBufs>::kThreads, 1)
-grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
+grouped_gemm_kernel(const __grid_constant__ P p) {
   using Cfg = GroupedCfg<kBN, kStages, kEpiWarps, kAccBufs>;
+  using Sched = Schedule<P, kBN>;
+  __shared__ typename Sched::Storage s_sched;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_full[kStages], bar_empty[kStages];
   __shared__ uint64_t bar_sf_landed[kStages], bar_sf_full[kStages];
@@ -132,6 +239,12 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
   griddep_wait();
   if (threadIdx.x == 0) griddep_launch_dependents();
   const AbortCtl ctl{&s_abort, p.status, p.wait_limit};
+  Sched sched(p, s_sched);
+  if constexpr (Sched::needs_fill()) {
+    sched.fill();
+    __syncthreads();
+  }
+  const int total_tiles = sched.tiles();
 
   if (warp == kProd) {
     // ------------------------------------------------------------ TMA producer
@@ -144,12 +257,12 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
       for (int s = 0; s < kStages; ++s) issued[s] = false, last_phase[s] = 0;
       bool ok = true;
       int prev_g = -1;
-      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
-        const GTile tc = grouped_tile(p, t);
-        const GroupInfo& gi = p.g[tc.g];
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const GTile tc = sched.tile(t);
+        const GroupView gi = sched.view(tc.g);
         if (tc.g != prev_g) {
-          tma_prefetch_desc(&p.tmap_a[tc.g]);
-          tma_prefetch_desc(&p.tmap_b[tc.g]);
+          tma_prefetch_desc(gi.tmap_a);
+          tma_prefetch_desc(gi.tmap_b);
           prev_g = tc.g;
         }
         const int k_blocks = gi.k / kBK;
@@ -183,8 +296,8 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
                       sfb_t + blk * (size_t)rest_k * kSfAtom + sf_off, kSfStageBytes, landed, pol);
           }
           mbar_arrive_expect_tx(full, Cfg::kABytes + Cfg::kBBytes);
-          tma_load_3d(sa, &p.tmap_a[tc.g], full, kb * 128, tc.mb * kBM, tc.l, pol);
-          tma_load_3d(sb, &p.tmap_b[tc.g], full, kb * 128, n0, tc.l, pol);
+          tma_load_3d(sa, gi.tmap_a, full, kb * 128, gi.a_row0 + tc.mb * kBM, tc.l, pol);
+          tma_load_3d(sb, gi.tmap_b, full, kb * 128, n0, tc.l, pol);
           issued[stage] = true;
           last_phase[stage] = phase;
           if (++stage == kStages) stage = 0, phase ^= 1u;
@@ -207,9 +320,9 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true, any = false;
-      for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
-        const GTile tc = grouped_tile(p, t);
-        const int k_blocks = p.g[tc.g].k / kBK;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const GTile tc = sched.tile(t);
+        const int k_blocks = sched.view(tc.g).k / kBK;
         if (!ctl.wait(smem_u32(&bar_acc_empty[acc]), acc_phase ^ 1u, kDevTimeoutAccFree)) {
           ok = false;
           break;
@@ -257,9 +370,9 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < p.tiles && ok; t += gridDim.x) {
-      const GTile tc = grouped_tile(p, t);
-      const int k_blocks = p.g[tc.g].k / kBK;
+    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+      const GTile tc = sched.tile(t);
+      const int k_blocks = sched.view(tc.g).k / kBK;
       for (int kb = 0; kb < k_blocks; ++kb) {
         bool got = true;
         if (lane == 0) got = ctl.wait(smem_u32(&bar_sf_landed[stage]), phase, kDevTimeoutTmaFull);
@@ -301,9 +414,9 @@ grouped_gemm_kernel(const __grid_constant__ GroupedParams<kMaxGroups> p) {
     constexpr int kChunks = kCW / 32;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int t = blockIdx.x; t < p.tiles; t += gridDim.x) {
-      const GTile tc = grouped_tile(p, t);
-      const GroupInfo& gi = p.g[tc.g];
+    for (int t = blockIdx.x; t < total_tiles; t += gridDim.x) {
+      const GTile tc = sched.tile(t);
+      const GroupView gi = sched.view(tc.g);
       if (!ctl.wait(smem_u32(&bar_acc_full[acc]), acc_phase, kDevTimeoutAccFull)) break;
       tc_fence_after();
       const uint32_t t_acc = tmem + ((uint32_t)(quad * 32) << 16) + acc * kBN + part * kCW;

@@ -29,6 +29,7 @@ EXPORTED = (
     "nvfp4_moe_workspace_bytes",
     "nvfp4_moe_sf_bytes",
     "nvfp4_moe_combine",
+    "nvfp4_moe_grouped_gemm",
     "nvfp4_device_status",
     "nvfp4_wait_selftest",
     "nvfp4_status_string",
@@ -91,6 +92,9 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
     lib.nvfp4_moe_sf_bytes.restype = sz
     lib.nvfp4_moe_combine.argtypes = [vp, i32, vp, vp, i32, i32, i32, vp, vp]
     lib.nvfp4_moe_combine.restype = i32
+    pp = ctypes.POINTER(ctypes.c_void_p)
+    lib.nvfp4_moe_grouped_gemm.argtypes = [vp, i32, vp, vp, vp, vp, pp, pp, i32, i32, i32, vp, vp]
+    lib.nvfp4_moe_grouped_gemm.restype = i32
     lib.nvfp4_device_status.argtypes = [vp, ctypes.POINTER(ctypes.c_uint)]
     lib.nvfp4_device_status.restype = i32
     lib.nvfp4_wait_selftest.argtypes = [ctypes.c_longlong, vp]

@@ -14,6 +14,7 @@ rows back to tokens (weighted sum over each token's choices).
 """
 from __future__ import annotations
 
+import ctypes
 from dataclasses import dataclass
 
 import torch
@@ -125,6 +126,53 @@ def grouped_inputs(d: Dispatch, weights, c_all: torch.Tensor, counts=None):
             which.append(e)
         row += m
     return (abc, sfab, sfab_perm, sizes), which
+
+
+class ExpertWeights:
+    """Per-expert NVFP4 weights for :func:`grouped_gemm`: ``w[e]`` = (b [N, K/2, 1]
+    float4_e2m1fn_x2 (or uint8 [N, K/2]), sfb_perm [32, 4, ceil(N/128), 4, K/64, 1]),
+    all on one device.  The pointer arrays for the C call are built once."""
+
+    def __init__(self, w):
+        self.w = list(w)
+        if not self.w:
+            raise ValueError("no experts")
+        b0 = self.w[0][0]
+        self.n, self.k = int(b0.shape[0]), int(b0.shape[1]) * 2
+        arr = ctypes.c_void_p * len(self.w)
+        for i, (b, sfb) in enumerate(self.w):
+            if tuple(b.shape[:2]) != (self.n, self.k // 2) or not b.is_cuda:
+                raise ValueError(f"expert {i}: weights must be CUDA [{self.n}, {self.k // 2}(, 1)]")
+            if b.stride(0) != self.k // 2 or b.stride(1) != 1 or b.device != b0.device:
+                raise ValueError(f"expert {i}: weights must be row-major [N][K/2] on {b0.device}")
+            rn, rk = -(-self.n // 128), self.k // 64
+            if sfb.numel() != rn * rk * 512 or sfb.device != b0.device:
+                raise ValueError(f"expert {i}: scales must hold {rn * rk * 512} bytes on {b0.device}")
+        self.b_ptrs = arr(*[b.data_ptr() for b, _ in self.w])
+        self.sfb_ptrs = arr(*[s.data_ptr() for _, s in self.w])
+
+    def __len__(self):
+        return len(self.w)
+
+
+def grouped_gemm(d: Dispatch, weights: ExpertWeights, c_all: torch.Tensor) -> torch.Tensor:
+    """C_e = A_e . W_eᵀ for every expert straight from the dispatch's device
+    sizes (no host synchronisation): expert e's output lands in rows
+    [row_offsets[e], +counts[e]) of ``c_all`` (fp16 [T*topk, N])."""
+    if len(weights) != d.experts or weights.k != d.k:
+        raise ValueError(f"weights are for {len(weights)} experts x K={weights.k}, "
+                         f"dispatch has {d.experts} x K={d.k}")
+    rows = d.tokens * d.topk
+    if (c_all.dtype != torch.float16 or tuple(c_all.shape) != (rows, weights.n)
+            or not c_all.is_contiguous() or c_all.device != d.packed.device):
+        raise ValueError(f"c_all must be a contiguous float16 [{rows}, {weights.n}] tensor "
+                         f"on {d.packed.device}")
+    lib = _lib.load()
+    _lib.check(on_device(c_all.device, lambda st: lib.nvfp4_moe_grouped_gemm(
+        d.packed.data_ptr(), rows, d.sf.data_ptr(), d.counts.data_ptr(), d.row_offsets.data_ptr(),
+        d.atom_offsets.data_ptr(), weights.b_ptrs, weights.sfb_ptrs, d.experts, weights.n, d.k,
+        c_all.data_ptr(), st)))
+    return c_all
 
 
 def combine(c_all: torch.Tensor, d: Dispatch, weights: torch.Tensor | None = None,

@@ -117,6 +117,24 @@ size_t nvfp4_moe_workspace_bytes(int tokens, int topk, int num_experts);
  * min(num_experts, tokens*topk)) * (K/64) * 512. */
 size_t nvfp4_moe_sf_bytes(int tokens, int topk, int k, int num_experts);
 
+/* Grouped GEMM over a dispatch without a host round trip: for every expert
+ * e < num_experts, C rows [row_offsets[e], +counts[e]) = A rows of the same
+ * range . B_eᵀ (fp16 out, fp32 accumulate), with A = a_packed (the
+ * dispatch's packed [a_rows][K/2] e2m1 rows), expert e's A scales the 128-row
+ * atom blocks of sfa_atoms from block atom_offsets[e], and b[e] / sfb_perm[e]
+ * (host arrays of device pointers) expert e's weights [N][K/2] and permuted
+ * scales.  counts / row_offsets / atom_offsets are the dispatch's DEVICE
+ * arrays: the kernel reads them when it runs, so dispatch, this GEMM and the
+ * combine can be enqueued (or captured in a CUDA graph) without reading the
+ * routing back.  c: fp16 [a_rows][N].  K % 256 == 0, N % 8 == 0.  Same
+ * arithmetic per tile as nvfp4_grouped_gemm.  No reference counterpart: the
+ * reference's grouped GEMM (nvfp4_group_gemm/submission_v7.py:454-522) takes
+ * host problem sizes. */
+int nvfp4_moe_grouped_gemm(const void* a_packed, int a_rows, const void* sfa_atoms,
+                           const int* counts, const int* row_offsets, const int* atom_offsets,
+                           const void* const* b, const void* const* sfb_perm, int num_experts,
+                           int n, int k, void* c, void* stream);
+
 /* MoE combine: out[t][n] = sum over j of weights[t*topk + j] *
  * c[dst[t*topk + j]][n] (fp32, j ascending, products and sums rounded
  * separately; pairs with dst < 0 or dst >= c_rows skipped; weights == NULL

@@ -137,3 +137,17 @@ def test_moe_sizes_and_rejections_without_gpu(lib):
     assert g(None, 10, p, None, 10, 1, 64, p, None) == _lib.NVFP4_ERR_INVALID_ARG
     assert g(p, 10, p, None, 0, 1, 64, p, None) == _lib.NVFP4_OK      # nothing to combine
     assert g(ctypes.c_void_p(4097), 10, p, None, 10, 1, 64, p, None) == _lib.NVFP4_ERR_ALIGNMENT
+
+
+def test_moe_grouped_gemm_rejects_without_gpu(lib):
+    p = ctypes.c_void_p(4096)
+    arr = (ctypes.c_void_p * 2)(4096, 4096)
+    f = lib.nvfp4_moe_grouped_gemm
+    assert f(p, 100, p, p, p, p, arr, arr, 2, 256, 300, p, None) == _lib.NVFP4_ERR_SHAPE   # K % 256
+    assert f(p, 100, p, p, p, p, arr, arr, 2, 250, 256, p, None) == _lib.NVFP4_ERR_SHAPE   # N % 8
+    assert f(p, 100, p, p, p, p, arr, arr, 0, 256, 256, p, None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert f(p, 0, p, p, p, p, arr, arr, 2, 256, 256, p, None) == _lib.NVFP4_OK       # no rows
+    bad = (ctypes.c_void_p * 2)(4096, None)
+    assert f(p, 100, p, p, p, p, arr, bad, 2, 256, 256, p, None) == _lib.NVFP4_ERR_INVALID_ARG
+    assert f(ctypes.c_void_p(4100), 100, p, p, p, p, arr, arr, 2, 256, 256, p, None) == \
+        _lib.NVFP4_ERR_ALIGNMENT

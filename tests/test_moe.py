@@ -237,3 +237,86 @@ def test_moe_layer_dispatch_grouped_combine():
     nbad, idx = O.allclose_report(out, ref, 1e-2, 1e-2)
     assert nbad == 0, idx
     assert which == [ex for ex in range(e) if counts[ex] > 0]
+
+
+def _moe_weights(e, n, k, seed):
+    from nvfp4_b200.formats import quantize_nvfp4, swizzle_sf
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for _ in range(e):
+        packed, sf = quantize_nvfp4(torch.randn(n, k, generator=g))
+        out.append((packed.view(torch.float4_e2m1fn_x2).unsqueeze(-1).cuda(),
+                    swizzle_sf(sf.unsqueeze(-1)).cuda()))
+    return out
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("t,topk,e,n,k,lo", [(600, 2, 6, 256, 512, 0), (333, 1, 5, 384, 256, -1),
+                                             (1000, 1, 3, 128, 512, 0), (50, 2, 130, 256, 256, 0)])
+def test_moe_grouped_gemm_matches_host_table_path(t, topk, e, n, k, lo):
+    """The device-routed grouped GEMM (sizes read on the device) gives exactly
+    the grouped GEMM of the host-table path on the same dispatch."""
+    from nvfp4_b200 import group_gemm as G
+    from nvfp4_b200 import moe
+    g = torch.Generator().manual_seed(t + e)
+    x = torch.randn(t, k, generator=g).cuda()
+    ids = torch.randint(lo, e, (t, topk), generator=g, dtype=torch.int32).cuda()
+    w = _moe_weights(e, n, k, seed=e)
+    d = moe.dispatch(x, ids, e)
+    c_dev = torch.full((t * topk, n), float("nan"), dtype=torch.float16, device="cuda")
+    moe.grouped_gemm(d, moe.ExpertWeights(w), c_dev)
+    c_host = torch.full((t * topk, n), float("nan"), dtype=torch.float16, device="cuda")
+    data, _ = moe.grouped_inputs(d, w, c_host)
+    G.custom_kernel(data)
+    rows = int(d.row_offsets[-1].item())
+    assert torch.equal(c_dev[:rows], c_host[:rows])
+    assert _lib_status() == 0
+
+
+def _lib_status():
+    from nvfp4_b200 import _lib
+    return _lib.device_status()
+
+
+@pytest.mark.gpu
+def test_moe_layer_captured_in_a_cuda_graph():
+    """dispatch -> device-routed grouped GEMM -> combine, captured once in a
+    CUDA graph (no host synchronisation inside) and replayed on new tokens
+    and new routing: equal to the eager layer on the same inputs."""
+    from nvfp4_b200 import moe
+    t, topk, e, n, k = 512, 2, 8, 256, 512
+    g = torch.Generator().manual_seed(21)
+    w = moe.ExpertWeights(_moe_weights(e, n, k, seed=3))
+    x = torch.randn(t, k, generator=g).cuda()
+    ids = torch.randint(0, e, (t, topk), generator=g, dtype=torch.int32).cuda()
+    rw = torch.rand(t, topk, generator=g).cuda()
+    d = moe.dispatch(x, ids, e)                            # buffers for the captured calls
+    c_all = torch.zeros(t * topk, n, dtype=torch.float16, device="cuda")
+    out = torch.zeros(t, n, dtype=torch.float32, device="cuda")
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        moe.dispatch(x, ids, e, out=d)
+        moe.grouped_gemm(d, w, c_all)
+        moe.combine(c_all, d, rw, out=out)
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=s):
+            moe.dispatch(x, ids, e, out=d)
+            moe.grouped_gemm(d, w, c_all)
+            moe.combine(c_all, d, rw, out=out)
+    for seed in (5, 6):
+        gg = torch.Generator().manual_seed(seed)
+        x.copy_(torch.randn(t, k, generator=gg))
+        ids.copy_(torch.randint(0, e, (t, topk), generator=gg, dtype=torch.int32))
+        rw.copy_(torch.rand(t, topk, generator=gg))
+        graph.replay()
+        torch.cuda.synchronize()
+        got = out.clone()
+        d2 = moe.dispatch(x, ids, e)
+        c2 = torch.zeros_like(c_all)
+        moe.grouped_gemm(d2, w, c2)
+        ref = moe.combine(c2, d2, rw)
+        torch.cuda.synchronize()
+        assert torch.equal(got, ref)
+    del graph
