@@ -133,6 +133,38 @@ def moe_workload(rank, world, device, tokens=32768):
     return (x, ids, experts, d), 0.0, nbytes, desc
 
 
+def moe_layer_workload(rank, world, device, tokens=32768):
+    """Configuration 7: the MoE expert layer around configuration 4's grouped
+    GEMM -- dispatch of 32768 fp32 tokens (Zipf top-1 over 64 experts),
+    device-routed grouped GEMM against 64 NVFP4 experts [2048 x 7168], weighted
+    combine -- with no host round trip inside the step.  Metric: the grouped
+    GEMM's FLOP over the whole layer's time."""
+    from nvfp4_b200 import inputs as I
+    from nvfp4_b200 import moe
+    from nvfp4_b200.quantize import quantize
+    spec = I.GROUP_CONFIGS[4]
+    k, n, experts = spec["k"], spec["n"], spec["experts"]
+    g = torch.Generator().manual_seed(7000 + rank)
+    weights = []
+    for _ in range(experts):
+        packed, _, sfp = quantize(torch.randn(n, k, generator=g).to(device))
+        weights.append((packed, sfp))
+    w = moe.ExpertWeights(weights)
+    x = torch.randn(tokens, k, generator=g).to(device)
+    ids = I.config4_expert_ids(seed=4 + rank, tokens=tokens).to(device)
+    rw = torch.rand(tokens, generator=g).to(device)
+    d = moe.dispatch(x, ids, experts)
+    c_all = torch.empty(tokens, n, dtype=torch.float16, device=device)
+    out = torch.empty(tokens, n, dtype=torch.float32, device=device)
+    torch.cuda.synchronize()
+    flop = 2.0 * tokens * n * k
+    nbytes = (tokens * k * 4 + tokens * 4 + experts * n * (k // 2 + k // 16)
+              + tokens * n * 4 + tokens * 4)          # tokens in, weights, out (the layer's I/O)
+    desc = dict(workload="moe_layer_cfg4", tokens=tokens, k=k, n=n, experts=experts, topk=1,
+                stages="dispatch + device-routed grouped GEMM + combine")
+    return (x, ids, rw, w, d, c_all, out), flop, nbytes, desc
+
+
 def shape_workload(args, device):
     """--shape M,N,K (dual) or --group-shape M1:M2:..,N,K (grouped): a seeded
     N(0,1) workload of any size for kernel-only profiling runs."""
@@ -158,6 +190,8 @@ def make_workload(cfg, rank, world, device, tokens=32768):
         return quant_workload(rank, world, device)
     if cfg == 6:
         return moe_workload(rank, world, device, tokens)
+    if cfg == 7:
+        return moe_layer_workload(rank, world, device, tokens)
     return dual_workload(cfg, rank, world, device) if cfg in (0, 1, 2) else \
         group_workload(cfg, rank, world, device)
 
@@ -170,6 +204,12 @@ def call(cfg, data):
         from nvfp4_b200 import moe
         x, ids, experts, d = data
         return moe.dispatch(x, ids, experts, out=d)
+    if cfg == 7:
+        from nvfp4_b200 import moe
+        x, ids, rw, w, d, c_all, out = data
+        moe.dispatch(x, ids, len(w), out=d)
+        moe.grouped_gemm(d, w, c_all)
+        return moe.combine(c_all, d, rw, out=out)
     if cfg in (0, 1, 2):
         from nvfp4_b200.dual_gemm import custom_kernel
     else:
@@ -184,6 +224,9 @@ def device_tensors(cfg, data):
     if cfg == 6:
         x, ids, _, d = data
         return [x, ids], [d.packed, d.sf, d.counts, d.row_offsets, d.atom_offsets, d.src, d.dst]
+    if cfg == 7:
+        x, ids, rw, _, _, _, out = data
+        return [x, ids, rw], [out]
     if cfg in (0, 1, 2):
         return [data[0], data[1], data[2], data[6], data[7], data[8]], [data[9]]
     abc, _, perm, sizes = data
@@ -353,6 +396,49 @@ def time_cpu_moe(x_dev, ids_dev, experts, budget_s: float):
                       f"{reps} reps (~{budget_s:.0f} s, single-threaded numpy)"}
 
 
+def time_cpu_moe_layer(data, budget_s: float, tokens: int = 256):
+    """Oracle MoE layer (numpy: route + quantise + per-expert dequantised fp32
+    GEMM + combine) on the first `tokens` tokens, TFLOP/s of the GEMM part."""
+    from oracle import nvfp4_oracle as O
+    x_dev, ids_dev, rw_dev, w = data[0], data[1], data[2], data[3]
+    x = x_dev[:tokens].detach().cpu().numpy()
+    ids = ids_dev[:tokens].detach().cpu().numpy().reshape(-1, 1)
+    rw = rw_dev[:tokens].detach().cpu().numpy()
+    used = sorted(set(int(v) for v in ids.reshape(-1)))
+    wts = {}
+    for e in used:
+        b, sfp = w.w[e]
+        n, kh = b.shape[0], b.shape[1]
+        wts[e] = (b.detach().cpu().view(torch.uint8).numpy().reshape(n, kh),
+                  O.unpermute_sf(sfp.detach().cpu().view(torch.uint8).permute(5, 2, 4, 0, 1, 3)
+                                 .contiguous().numpy(), n, kh * 2 // 16)[:, :, 0])
+    n = next(iter(wts.values()))[0].shape[0]
+    k = x.shape[1]
+
+    def step():
+        (counts, row_off, _, src, dst), packed, _ = O.moe_dispatch(x, ids, len(w.w))
+        _, sf = O.quantize_nvfp4(x[src])
+        c = np.zeros((len(src), n), np.float16)
+        for e in used:
+            r0, r1 = int(row_off[e]), int(row_off[e + 1])
+            if r1 > r0:
+                c[r0:r1] = O.ref_group(packed[r0:r1], wts[e][0], sf[r0:r1], wts[e][1])
+        O.moe_combine(c, dst, rw, x.shape[0], 1)
+
+    torch.set_num_threads(cpu_cores())
+    step()
+    secs, reps = 0.0, 0
+    while reps < 1 or secs < budget_s:
+        t0 = time.perf_counter()
+        step()
+        secs += time.perf_counter() - t0
+        reps += 1
+    return {"value": round(2.0 * tokens * n * k * reps / secs / 1e12, 5), "unit": "TFLOP/s",
+            "cores": cpu_cores(), "kind": "port",
+            "sample": f"numpy oracle MoE layer (route, quantise, dequantised fp32 GEMM per expert, "
+                      f"combine) on {tokens} tokens x K={k} x N={n}, {reps} reps (~{budget_s:.0f} s)"}
+
+
 def cpu_cores():
     try:
         return len(os.sched_getaffinity(0))
@@ -476,6 +562,8 @@ def metric_name(cfg):
         return "NVFP4 quantisation bandwidth (fp32 -> e2m1 + e4m3 scales)"
     if cfg == 6:
         return "MoE dispatch bandwidth (route + fp32 -> NVFP4 per-expert operands)"
+    if cfg == 7:
+        return "NVFP4 effective TFLOPS (MoE expert layer: dispatch + grouped GEMM + combine)"
     return "NVFP4 effective TFLOPS (dual GEMM)" if cfg in (0, 1, 2) else \
         "NVFP4 effective TFLOPS (grouped GEMM)"
 
@@ -485,9 +573,10 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4, 5, 6],
+    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4, 5, 6, 7],
                     help="0-4: BASELINE configurations; 5: device quantisation of config 1's "
-                         "operands; 6: MoE dispatch of config 4's routing")
+                         "operands; 6: MoE dispatch of config 4's routing; 7: the MoE expert "
+                         "layer around config 4")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--cpu-budget", type=float, default=12.0)
@@ -638,24 +727,27 @@ def main():
         "metric": metric_name(cfg), "value": round(value, 2), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 5), "us_per_call": round(ms_per_step * 1e3, 2),
-        "higher_is_better": True, "scaling": "weak" if cfg in (0, 1, 2, 6) else "strong",
+        "higher_is_better": True, "scaling": "weak" if cfg in (0, 1, 2, 6, 7) else "strong",
         "vs_baseline": None,
         "dtype": ("int32 routing + fp32 -> e2m1 + e4m3 block16" if cfg == 6 else
                   "fp32 -> e2m1 + e4m3 block16") if quant
+        else "fp32 tokens -> nvfp4 x nvfp4 -> fp32 acc -> fp16 -> fp32 combine" if cfg == 7
         else "nvfp4(e2m1+e4m3 block16) x nvfp4 -> fp32 acc -> fp16",
         "data": "synthetic: seeded N(0,1) fp32 quantised to NVFP4",
-        "config": {**desc, "parallelism": f"{'n-shard' if cfg in (0, 1, 2) else 'token-shard' if cfg == 6 else 'expert-lpt'}{world}",
+        "config": {**desc, "parallelism": f"{'n-shard' if cfg in (0, 1, 2) else 'token-shard' if cfg in (6, 7) else 'expert-lpt'}{world}",
                    "l2": f"flushed ({L2_FLUSH_BYTES >> 20} MiB write) between timed calls"},
         "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
                 "api": "nvfp4_b200.*.custom_kernel (ctypes -> libnvfp4_b200.so)"},
         "roofline": roof,
-        "gpu_launches": args.steps * (4 if cfg == 6 else len(data) if quant else 1),
+        "gpu_launches": args.steps * (4 if cfg == 6 else 6 if cfg == 7 else len(data) if quant else 1),
         "clocks": clk.summary(),
     }
 
     if rank == 0 and world == 1 and not args.no_cpu_baseline and cfg == 6:
         result["cpu_baseline"] = time_cpu_moe(data[0], data[1], data[2], args.cpu_budget)
+    elif rank == 0 and world == 1 and not args.no_cpu_baseline and cfg == 7:
+        result["cpu_baseline"] = time_cpu_moe_layer(data, args.cpu_budget)
     elif rank == 0 and world == 1 and not args.no_cpu_baseline and quant:
         result["cpu_baseline"] = time_cpu_quant(data[0][0], args.cpu_budget)
     elif rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -681,6 +773,8 @@ def run_reference_arm(args, cfg, rank, world):
     from nvfp4_b200 import inputs as I
     if cfg in (5, 6):
         return run_reference_bytes_arm(args, cfg, world)
+    if cfg == 7:
+        return run_reference_layer_arm(args, world)
     if cfg in (0, 1, 2):
         spec = I.DUAL_CONFIGS[cfg]
         g = torch.Generator().manual_seed(spec["seed"])
@@ -726,6 +820,45 @@ def run_reference_arm(args, cfg, rank, world):
         "cpu_baseline": {"value": round(v, 5), "unit": "TFLOP/s", "cores": cpu_cores(),
                          "kind": "port", "sample": sample},
         "e2e": {"value": round(v, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def run_reference_layer_arm(args, world, tokens: int = 128):
+    """Configuration 7 on the host: the numpy oracle MoE layer on the first
+    `tokens` tokens of configuration 4's routing (weights quantised on the
+    host for the experts the sample touches)."""
+    import types
+    from nvfp4_b200 import inputs as I
+    from nvfp4_b200.formats import quantize_nvfp4, swizzle_sf
+    spec = I.GROUP_CONFIGS[4]
+    k, n, experts = spec["k"], spec["n"], spec["experts"]
+    g = torch.Generator().manual_seed(7000)
+    ids = I.config4_expert_ids(tokens=32768)[:tokens]
+    used = set(int(v) for v in ids)
+    ws = []
+    for e in range(experts):
+        wf = torch.randn(n, k, generator=g)
+        if e in used:
+            p8, sf = quantize_nvfp4(wf)
+            ws.append((p8.view(torch.float4_e2m1fn_x2).unsqueeze(-1), swizzle_sf(sf.unsqueeze(-1))))
+        else:
+            ws.append(None)
+    w = types.SimpleNamespace(w=ws, n=n)
+    x = torch.randn(tokens, k, generator=g)
+    rw = torch.rand(tokens, generator=g)
+    budget = max(1.0, 150.0 / max(1, args.steps))
+    runs = [time_cpu_moe_layer((x, ids, rw, w), budget, tokens=tokens) for _ in range(args.steps)]
+    v = statistics.mean(r["value"] for r in runs)
+    print(json.dumps({
+        "impl": "reference", "metric": metric_name(7), "value": round(v, 6), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(budget * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32 (dequantised nvfp4)",
+        "data": "synthetic: seeded N(0,1) fp32, configuration 4 routing",
+        "config": {"workload": "moe_layer_cfg4", "sample_tokens": tokens, "budget_s": budget},
+        "cpu_baseline": {**runs[0], "value": round(v, 6)},
+        "e2e": {"value": round(v, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
 
