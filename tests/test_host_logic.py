@@ -135,3 +135,42 @@ def test_multi_rank_reduction_gloo():
     assert all(p.exitcode == 0 for p in procs)
     t, f = q.get(timeout=5)
     assert t == 2.0 and f == 30.0          # max time over ranks, summed work
+
+
+def _failing_rank_main(rank, world, port, out):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=20))
+    if rank == 1:
+        # a step fails on this rank: it leaves between steps, before the barrier
+        out.put((rank, "raised"))
+        dist.destroy_process_group()
+        return
+    try:
+        dist.monitored_barrier(timeout=datetime.timedelta(seconds=3))
+        out.put((rank, "barrier passed"))
+    except RuntimeError as e:
+        out.put((rank, "error: " + str(e).splitlines()[0][:200]))
+    finally:
+        try:
+            dist.destroy_process_group()
+        except Exception:
+            pass
+
+
+def test_rank_failure_surfaces_as_error_not_hang():
+    """A rank that fails between steps (and leaves) is reported to the others
+    by the next barrier with a timeout, as an exception within seconds."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = 31500 + os.getpid() % 1000
+    procs = [ctx.Process(target=_failing_rank_main, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=90)
+    assert all(not p.is_alive() for p in procs), "a rank hung"
+    got = dict(q.get(timeout=5) for _ in range(2))
+    assert got[1] == "raised"
+    assert got[0].startswith("error"), got[0]
