@@ -432,7 +432,7 @@ int launch_dual(DeviceState* d, int slot, DualParams& p, int forced_splits, int 
                      "dual_gemm_kernel");
 }
 
-// CTA-pair kernel with 96-column tiles, 192-wide MMAs and two accumulator buffers.
+// CTA-pair kernel: kBN-column tiles (128 or 96), M=256 x N=2*kBN MMAs, one accumulator.
 template <int kBN, int kStages>
 int launch_dual_2sm(DeviceState* d, int slot, const void* a, const void* b1, const void* b2,
                     const void* sfa, const void* sfb1, const void* sfb2, void* c, int m, int n,

@@ -1,38 +1,36 @@
-// NVFP4 dual GEMM on CTA pairs with 192-wide MMAs and double-buffered
-// accumulators, sm_100a: the large-problem kernel.
+// NVFP4 dual GEMM on CTA pairs (tcgen05.mma.cta_group::2), sm_100a.
 //
 //   C = silu(A . B1ᵀ) * (A . B2ᵀ)   (fp32 accumulate in TMEM, fp16 out)
 //
 // Same computation as the reference's ref_kernel
 // (nvfp4_dual_gemm/reference.py:27-77); own design:
 //
-// * a CTA pair (cluster of 2 on neighbouring SMs) owns a 256 x 96 tile of C.
-//   CTA r holds A rows [256*mp + 128*r, +128) and one 96-row B tile: CTA 0
-//   the B1 rows of the tile's columns, CTA 1 the B2 rows.  One
-//   tcgen05.mma.cta_group::2 with M = 256, N = 192 per 64-deep K step then
-//   writes, in each CTA's TMEM, its 128 rows x [gate 96 | up 96].  Per SM
-//   and K step: A 16 KB + B 12 KB of operands for 128 x 192 outputs (the
-//   single-CTA kernel: 48 KB for 128 x 256), and one MMA instruction covers
-//   both SMs;
-// * one 192-column accumulator; eight epilogue warps pull all of it into
-//   registers (48 gate + 48 up columns per warp) and release it before the
-//   math and the stores, so the next tile's MMAs start early;
-// * scale factors: each CTA bulk-loads its A atoms and the atom blocks that
-//   cover the tile's 96 B1 and 96 B2 rows (a 96-row tile need not start on a
-//   128-row atom) onto a landing barrier; four staging warps per CTA gather
-//   row i of every needed atom column into TMEM lane i of each quadrant with
-//   tcgen05.st (SFA: 4 columns per K step; SFB: columns c = 0..5 hold B rows
-//   32c..32c+31 of the 192-row MMA operand) and arrive on the leader's
-//   per-stage barrier.  Each pipeline stage owns one TMEM scale buffer (48
-//   columns): refilling a stage already waits for the MMAs that read it.
-//   (Two accumulator buffers would leave room for only two scale buffers,
-//   which put the commit -> staging -> MMA chain on every K block's critical
-//   path: 2.6x slower, measured.);
+// * a CTA pair (cluster of 2 on neighbouring SMs) owns a 256 x kBN tile of C
+//   (kBN = 128, or 96).  CTA r holds A rows [256*mp + 128*r, +128) and one
+//   kBN-row B tile: CTA 0 the B1 rows of the tile's columns, CTA 1 the B2
+//   rows.  One tcgen05.mma.cta_group::2 with M = 256, N = 2*kBN per 64-deep
+//   K step then writes, in each CTA's TMEM, its 128 rows x [gate kBN | up
+//   kBN].  Per SM and K step: A 16 KB + B 16 KB of operands for 128 x kBN
+//   outputs (the single-CTA kernel: 48 KB for 128 x 128 outputs), and one
+//   MMA instruction covers both SMs;
+// * one accumulator; eight epilogue warps per CTA pull their gate and up
+//   columns into registers and release the accumulator (remote arrives on
+//   the leader's barrier) before the math and the stores;
+// * scale factors: each CTA bulk-loads its A atoms and the B1 / B2 atom
+//   blocks covering the tile onto a landing barrier; four staging warps per
+//   CTA write them into TMEM with tcgen05.st (SFA: 4 columns per K step;
+//   SFB: column 8j + c holds B rows 32c..32c+31 of the 2*kBN-row operand,
+//   whole atom rows for 128-wide tiles, gathered 4-byte columns for 96-wide
+//   ones) and arrive on the leader's per-stage barrier.  Each pipeline stage
+//   owns one TMEM scale buffer: refilling a stage already waits for the
+//   MMAs that read it;
 // * both producers count their tile bytes on the leader's stage barrier
 //   (TMA .cta_group::2, no multicast); the leader commits to both CTAs
-//   (tcgen05.commit multicast); epilogue warps of both CTAs release an
-//   accumulator buffer with arrivals on the leader's barrier; cluster
-//   barriers bracket setup and teardown.  All waits are bounded.
+//   (tcgen05.commit multicast); cross-CTA handshakes use CTA-scope-release
+//   remote arrives; cluster barriers bracket setup and teardown.  All waits
+//   are bounded.  The second CTA of the last pair block may lie wholly past
+//   M: its A rows load as zeros, it stores nothing, and it re-reads the last
+//   real A-scale block.
 #pragma once
 #include <cuda.h>
 #include "kernel_common.cuh"
@@ -41,14 +39,14 @@ namespace nvfp4 {
 
 struct Dual2smParams {
   CUtensorMap tmap_a;    // bytes [L][M][K/2], box {128 B, 128 rows, 1}
-  CUtensorMap tmap_b1;   // bytes [L][N][K/2], box {128 B, 96 rows, 1}
+  CUtensorMap tmap_b1;   // bytes [L][N][K/2], box {128 B, kBN rows, 1}
   CUtensorMap tmap_b2;
   const uint8_t* sfa;    // permuted scale atoms [L][ceil(M/128)][K/64][512]
   const uint8_t* sfb1;   // [L][ceil(N/128)][K/64][512]
   const uint8_t* sfb2;
   __half* c;             // [L][M][N]
   int m, n, k, l;
-  int mp_blocks, n_blocks, k_blocks, tiles;  // 256-row pair blocks, 96-column blocks
+  int mp_blocks, n_blocks, k_blocks, tiles;  // 256-row pair blocks, kBN-column blocks
   int sfa_blocks, sfb_blocks;                // ceil(M/128), ceil(N/128)
   int group_m;                               // raster: pair M-blocks per group
   int c_lines32;                             // C rows start 32-byte aligned
@@ -77,7 +75,7 @@ struct Dual2smCfg {
   static constexpr int kTmemCols = 512;
   static constexpr int kAccBufs = 1;
   static constexpr int kAccCols = kNmma;
-  static constexpr int kSfCol = kAccBufs * kAccCols;   // 192
+  static constexpr int kSfCol = kAccBufs * kAccCols;   // 2 * kBN
   static constexpr int kSfBufCols = 48;                // per stage: SFA 4x4 + SFB 4x8 (6 used)
   static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned");
   static_assert(kSfCol + kStages * kSfBufCols <= kTmemCols, "TMEM budget: one scale buffer per stage");
@@ -221,7 +219,7 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (leader && lane == 0) {
       constexpr uint32_t idesc = (1u << 7) | (1u << 10) | ((uint32_t)(Cfg::kNmma >> 3) << 17) |
-                                 ((uint32_t)(256 >> 4) << 24);   // M=256, N=192, e2m1 x e2m1, e4m3 scales
+                                 ((uint32_t)(256 >> 4) << 24);   // M=256, N=2*kBN, e2m1 x e2m1, e4m3 scales
       constexpr uint16_t kBoth = 0x3;
       int stage = 0;
       uint32_t phase = 0;
