@@ -214,6 +214,56 @@ def test_group_task_shapes(case, bn, monkeypatch):
         assert_close(got.cpu().numpy(), want, f"group case {case} g{i}")
 
 
+GROUP_TASK_BENCH = [  # nvfp4_group_gemm/task.yml:59-63 (m per group, n, k)
+    ([80, 176, 128, 72, 64, 248, 96, 160], 4096, 7168), ([40, 76, 168, 72, 164, 148, 196, 160], 7168, 2048),
+    ([192, 320], 3072, 4096), ([128, 384], 4096, 1536),
+]
+
+
+@pytest.mark.parametrize("bn", ["128", "auto"])
+@pytest.mark.parametrize("case", range(len(GROUP_TASK_BENCH)))
+def test_group_benchmark_shapes(case, bn, monkeypatch):
+    if bn != "auto":
+        monkeypatch.setenv("NVFP4_GROUPED_BN", bn)
+    ms, n, k = GROUP_TASK_BENCH[case]
+    data = I.generate_group_input(ms, [n] * len(ms), [k] * len(ms), len(ms), seed=1111, device="cuda")
+    outs = G.custom_kernel(data)
+    assert _lib.device_status() == 0
+    # the widest group in full, sampled rows of the others
+    abc, sfab, _, sizes = data
+    wide = max(range(len(ms)), key=lambda i: ms[i])
+    for i in range(len(ms)):
+        (a, b, _), (sa, sb) = abc[i], sfab[i]
+        rows = torch.arange(0, ms[i], 1 if i == wide else 13)
+        want = O.ref_group(_np(_rows(a, rows))[:, :, 0], _np(b)[:, :, 0],
+                           _np(_rows(sa, rows))[:, :, 0], _np(sb)[:, :, 0])
+        assert_close(outs[i][rows.to(outs[i].device), :, 0].cpu().numpy(), want,
+                     f"benchmark group case {case} g{i}")
+
+
+def test_group_ragged_k_and_chunks():
+    # groups of different K (tiles of 2..12 K blocks), ragged M and N, zero-M
+    # groups, and more groups than one launch holds
+    gen = torch.Generator().manual_seed(31)
+    shapes = [(0, 256, 512), (200, 264, 1536), (72, 512, 256), (0, 256, 768), (384, 256, 768)]
+    shapes += [(8 * (i % 9 + 1), 256 + 8 * (i % 3), 256 * (i % 4 + 1)) for i in range(100)]
+    pairs = [(torch.randn(m, k, generator=gen), torch.randn(n, k, generator=gen)) for m, n, k in shapes]
+    data = I.group_from_fp32(pairs, device="cuda")
+    outs = G.custom_kernel(data)
+    assert _lib.device_status() == 0
+    for i, (got, want) in enumerate(zip(outs, oracle_group(data))):
+        assert_close(got.cpu().numpy(), want, f"group g{i} {shapes[i]}")
+
+
+def test_group_deterministic():
+    ms, n, k = GROUP_TASK_BENCH[0]
+    data = I.generate_group_input(ms, [n] * len(ms), [k] * len(ms), len(ms), seed=9, device="cuda")
+    runs = [[o.clone() for o in G.custom_kernel(data)] for _ in range(3)]
+    assert _lib.device_status() == 0
+    for r in runs[1:]:
+        assert all(torch.equal(x, y) for x, y in zip(runs[0], r))
+
+
 def test_group_zero_and_many_groups():
     # a zero-M group, ragged M, and more groups than one 16-entry launch holds
     ms = [0, 64, 40, 0, 200, 128] + [8 * (i + 1) for i in range(14)]
