@@ -29,7 +29,6 @@ import json
 import os
 import statistics
 import sys
-import threading
 import time
 from pathlib import Path
 
@@ -246,64 +245,89 @@ def nbytes_of(ts):
 # ---------------------------------------------------------------------------
 # clocks (NVML, read-only)
 # ---------------------------------------------------------------------------
+# The sampler loop runs in a child process, every 100 ms: NVML queries go
+# through the driver like the kernel launches, and sampling every 1 ms (from
+# a thread of this process, or from a child) stalled the launch loop often
+# enough to put a ~40 us/call outlier batch into one benchmark shape.
+_SAMPLER_SRC = r"""
+import select, sys
+import pynvml
+pynvml.nvmlInit()
+bus, index, period = sys.argv[1], int(sys.argv[2]), float(sys.argv[3])
+try:
+    h = pynvml.nvmlDeviceGetHandleByPciBusId_v2(bus)
+except Exception:
+    h = pynvml.nvmlDeviceGetHandleByIndex(index)
+reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+    pynvml.nvmlDeviceGetCurrentClocksThrottleReasons
+print("ready", pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM), flush=True)
+out = []
+while not select.select([sys.stdin], [], [], period)[0]:   # until the parent closes stdin
+    try:
+        out.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM), reasons(h)))
+    except Exception:
+        pass
+print("\n".join(f"{m} {r}" for m, r in out), flush=True)
+"""
+
+
 class ClockSampler:
+    """SM clock and clock-event reasons of one GPU, sampled every `period_s`
+    by NVML in a child process while the `with` block runs."""
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
                "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, device_index: int, period_s: float = 0.001):
+    def __init__(self, device_index: int, period_s: float = 0.1):
         self.samples, self.reasons = [], set()
         self.ok = False
+        self.err = None
+        self.max_mhz = None
+        self.proc = None
         try:
-            import pynvml
-            pynvml.nvmlInit()
-            self.nv = pynvml
-            self.h = self._handle(pynvml, device_index)
-            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            pr = torch.cuda.get_device_properties(device_index)
+            self.bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+        except Exception:  # noqa: BLE001
+            self.bus = ""
+        self.index = device_index
+        self.period = period_s
+
+    def __enter__(self):
+        import subprocess
+        try:
+            self.proc = subprocess.Popen(
+                [sys.executable, "-c", _SAMPLER_SRC, self.bus, str(self.index), str(self.period)],
+                stdin=subprocess.PIPE, stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+            first = self.proc.stdout.readline().split()
+            if len(first) != 2 or first[0] != "ready":
+                raise RuntimeError("sampler did not start: " + self.proc.stderr.read()[-300:])
+            self.max_mhz = int(first[1])
             self.ok = True
         except Exception as e:  # noqa: BLE001
             self.err = repr(e)
-        self.period = period_s
-        self._stop = threading.Event()
-
-    @staticmethod
-    def _handle(nv, device_index):
-        """NVML handle of the CUDA device (matched by PCI id, so it also works
-        under CUDA_VISIBLE_DEVICES)."""
-        try:
-            pr = torch.cuda.get_device_properties(device_index)
-            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
-            return nv.nvmlDeviceGetHandleByPciBusId_v2(bus)
-        except Exception:  # noqa: BLE001
-            return nv.nvmlDeviceGetHandleByIndex(device_index)
-
-    def _reasons(self):
-        nv = self.nv
-        fn = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
-            getattr(nv, "nvmlDeviceGetCurrentClocksThrottleReasons")
-        return fn(self.h)
-
-    def _run(self):
-        while not self._stop.is_set():
-            try:
-                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
-                bits = self._reasons()
-                for name, b in self.REASONS.items():
-                    if bits & b:
-                        self.reasons.add(name)
-            except Exception:  # noqa: BLE001
-                pass
-            time.sleep(self.period)
-
-    def __enter__(self):
-        if self.ok:
-            self.t = threading.Thread(target=self._run, daemon=True)
-            self.t.start()
+            if self.proc is not None and self.proc.poll() is None:
+                self.proc.kill()
+                self.proc.wait()
         return self
 
     def __exit__(self, *exc):
-        if self.ok:
-            self._stop.set()
-            self.t.join()
+        if not self.ok:
+            return
+        try:
+            out, _ = self.proc.communicate(input="", timeout=30)
+        except Exception as e:  # noqa: BLE001
+            self.proc.kill()
+            self.proc.wait()
+            self.ok, self.err = False, repr(e)
+            return
+        for line in out.split("\n"):
+            f = line.split()
+            if len(f) != 2:
+                continue
+            self.samples.append(int(f[0]))
+            bits = int(f[1])
+            for name, b in self.REASONS.items():
+                if bits & b:
+                    self.reasons.add(name)
 
     def summary(self):
         if not self.ok:
@@ -519,7 +543,7 @@ def run_task_suite(args):
     device = torch.device("cuda", 0)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     for kind, shapes, fn in (("dual", TASK_DUAL, dual_kernel), ("group", TASK_GROUP, group_kernel)):
-        per_shape, tflops = [], []
+        per_shape, per_shape_std, tflops = [], [], []
         with ClockSampler(0) as clk:
             for shape in shapes:
                 datas = task_inputs(kind, shape, device)
@@ -539,6 +563,7 @@ def run_task_suite(args):
                     times.append(e0.elapsed_time(e1) * 1e3 / len(datas))
                 us = statistics.mean(times)
                 per_shape.append(round(us, 3))
+                per_shape_std.append(round(statistics.stdev(times), 3) if len(times) > 1 else 0.0)
                 tflops.append(round(task_flop(kind, shape) / us / 1e6, 1))
                 del datas
         assert _lib.device_status() == 0
@@ -549,7 +574,7 @@ def run_task_suite(args):
                       f"({'dual' if kind == 'dual' else 'grouped'} GEMM)",
             "value": round(geo, 3), "unit": "us", "higher_is_better": False,
             "vs_baseline": round(geo / pub, 4), "reference_published_us": pub,
-            "per_shape_us": per_shape, "per_shape_tflops": tflops,
+            "per_shape_us": per_shape, "per_shape_std_us": per_shape_std, "per_shape_tflops": tflops,
             "shapes": [list(s) if kind == "dual" else [s[0], s[1], s[2]] for s in shapes],
             "method": f"{TASK_INPUTS} distinct seeded inputs per shape (reference generator "
                       f"distributions), L2 flushed before each batch, mean per call over "
@@ -749,6 +774,7 @@ def main():
         "metric": metric_name(cfg), "value": round(value, 2), "unit": unit,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms_per_step, 5), "us_per_call": round(ms_per_step * 1e3, 2),
+        "us_per_call_std": round(statistics.stdev(per_call_ms) * 1e3, 2) if len(per_call_ms) > 1 else 0.0,
         "higher_is_better": True, "scaling": "weak" if cfg in (0, 1, 2, 6, 7) else "strong",
         "vs_baseline": None,
         "dtype": ("int32 routing + fp32 -> e2m1 + e4m3 block16" if cfg == 6 else

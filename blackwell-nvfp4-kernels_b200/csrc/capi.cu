@@ -500,9 +500,9 @@ int launch_grouped_chunk(DeviceState* d, int slot, const nvfp4_group* gs, const 
                      "grouped_gemm_kernel");
 }
 
-// 128x256 tiles (4 stages, 8 epilogue warps, one accumulator buffer) when
-// every group is at least 256 wide, else 128x128 tiles (6 stages, 4 epilogue
-// warps, two accumulator buffers).
+// bn 256: 128x256 tiles (4 stages, 8 epilogue warps, one accumulator
+// buffer); bn 128: 128x128 tiles (6 stages, 4 epilogue warps, two
+// accumulator buffers).
 template <int kMaxGroups>
 int launch_grouped(DeviceState* d, const nvfp4_group* gs, const int* idx, int count, int bn,
                    cudaStream_t stream) {
@@ -649,9 +649,19 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
   if (rc) return rc;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_);
   const int n = (int)live.size();
+  // 128x256 tiles when every group is at least 256 wide, unless all the
+  // 128x128 tiles fit in one wave: a 128-wide K block costs ~0.74 of a
+  // 256-wide one (the copy path moves 36 instead of 54 KB), so a one-wave
+  // grid of them finishes first (measured 149.7 vs 101.1 us on configuration
+  // 3, twice the tiles, 0.74 per K block).
   int min_n = groups[live[0]].n;
-  for (int i : live) min_n = groups[i].n < min_n ? groups[i].n : min_n;
-  int bn = min_n >= 256 ? 256 : 128;
+  long long tiles128 = 0;
+  for (int i : live) {
+    const nvfp4_group& g = groups[i];
+    min_n = g.n < min_n ? g.n : min_n;
+    tiles128 += (long long)g.l * ((g.m + kBM - 1) / kBM) * ((g.n + 127) / 128);
+  }
+  int bn = min_n >= 256 && tiles128 > d->num_sms ? 256 : 128;
   const Knobs kn = read_knobs();
   t_pdl = kn.pdl;
   const int forced = kn.grouped_bn;
