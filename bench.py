@@ -25,6 +25,8 @@ the data path); grouped configurations assign experts by LPT (strong scaling).
 from __future__ import annotations
 
 import argparse
+import contextlib
+import gc
 import json
 import os
 import statistics
@@ -41,6 +43,22 @@ import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+@contextlib.contextmanager
+def gc_paused():
+    """Python's cyclic garbage collector collected before and paused over a
+    timed region (as `timeit` does): a collection triggered by allocation
+    counts inside the region stalls the launch loop for up to milliseconds,
+    idling the GPU inside a timed batch."""
+    gc.collect()
+    was = gc.isenabled()
+    gc.disable()
+    try:
+        yield
+    finally:
+        if was:
+            gc.enable()
 L2_FLUSH_BYTES = 512 << 20
 
 
@@ -245,10 +263,9 @@ def nbytes_of(ts):
 # ---------------------------------------------------------------------------
 # clocks (NVML, read-only)
 # ---------------------------------------------------------------------------
-# The sampler loop runs in a child process, every 100 ms: NVML queries go
-# through the driver like the kernel launches, and sampling every 1 ms (from
-# a thread of this process, or from a child) stalled the launch loop often
-# enough to put a ~40 us/call outlier batch into one benchmark shape.
+# The sampler loop runs in a child process (a sampling thread here would
+# compete with the launch loop for the GIL); NVML queries also go through the
+# driver like the launches, so the period is a few milliseconds, not one.
 _SAMPLER_SRC = r"""
 import select, sys
 import pynvml
@@ -277,7 +294,7 @@ class ClockSampler:
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
                "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, device_index: int, period_s: float = 0.1):
+    def __init__(self, device_index: int, period_s: float = 0.005):
         self.samples, self.reasons = [], set()
         self.ok = False
         self.err = None
@@ -544,7 +561,7 @@ def run_task_suite(args):
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
     for kind, shapes, fn in (("dual", TASK_DUAL, dual_kernel), ("group", TASK_GROUP, group_kernel)):
         per_shape, per_shape_std, tflops = [], [], []
-        with ClockSampler(0) as clk:
+        with ClockSampler(0, period_s=0.02) as clk:
             for shape in shapes:
                 datas = task_inputs(kind, shape, device)
                 for _ in range(args.warmup):
@@ -552,15 +569,17 @@ def run_task_suite(args):
                         fn(d)
                 torch.cuda.synchronize()
                 times = []
-                for _ in range(args.steps):
-                    flush.zero_()
-                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                    e0.record()
-                    for d in datas:
-                        fn(d)
-                    e1.record()
-                    torch.cuda.synchronize()
-                    times.append(e0.elapsed_time(e1) * 1e3 / len(datas))
+                with gc_paused():
+                    for _ in range(args.steps):
+                        flush.zero_()
+                        e0 = torch.cuda.Event(enable_timing=True)
+                        e1 = torch.cuda.Event(enable_timing=True)
+                        e0.record()
+                        for d in datas:
+                            fn(d)
+                        e1.record()
+                        torch.cuda.synchronize()
+                        times.append(e0.elapsed_time(e1) * 1e3 / len(datas))
                 us = statistics.mean(times)
                 per_shape.append(round(us, 3))
                 per_shape_std.append(round(statistics.stdev(times), 3) if len(times) > 1 else 0.0)
@@ -658,7 +677,7 @@ def main():
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local) as clk:
+    with ClockSampler(local) as clk, gc_paused():
         torch.cuda.nvtx.range_push("timed")
         for i in range(args.steps):
             flush.zero_()                       # evict L2 between calls (outside the events)
@@ -715,32 +734,33 @@ def main():
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
-    es.record(stream)
-    s_in.wait_event(es)
-    s_out.wait_event(es)
-    done_out = None
-    for _ in range(args.e2e_steps):
-        with torch.cuda.stream(s_in):              # inputs are free once the last compute ended
-            s_in.wait_stream(stream)
-            for d, h in zip(ins, h_ins):
-                d.copy_(h, non_blocking=True)
-            ev_in = torch.cuda.Event()
-            ev_in.record(s_in)
-        stream.wait_event(ev_in)
-        if done_out is not None:
-            stream.wait_event(done_out)
-        call(cfg, data)
-        ev_c = torch.cuda.Event()
-        ev_c.record(stream)
-        with torch.cuda.stream(s_out):
-            s_out.wait_event(ev_c)
-            for h, d in zip(h_outs, outs):
-                h.copy_(d, non_blocking=True)
-            done_out = torch.cuda.Event()
-            done_out.record(s_out)
-    stream.wait_event(done_out)
-    ee.record(stream)
-    torch.cuda.synchronize()
+    with gc_paused():
+        es.record(stream)
+        s_in.wait_event(es)
+        s_out.wait_event(es)
+        done_out = None
+        for _ in range(args.e2e_steps):
+            with torch.cuda.stream(s_in):              # inputs are free once the last compute ended
+                s_in.wait_stream(stream)
+                for d, h in zip(ins, h_ins):
+                    d.copy_(h, non_blocking=True)
+                ev_in = torch.cuda.Event()
+                ev_in.record(s_in)
+            stream.wait_event(ev_in)
+            if done_out is not None:
+                stream.wait_event(done_out)
+            call(cfg, data)
+            ev_c = torch.cuda.Event()
+            ev_c.record(stream)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_c)
+                for h, d in zip(h_outs, outs):
+                    h.copy_(d, non_blocking=True)
+                done_out = torch.cuda.Event()
+                done_out.record(s_out)
+        stream.wait_event(done_out)
+        ee.record(stream)
+        torch.cuda.synchronize()
     e2e_t = torch.tensor([es.elapsed_time(ee) / 1e3], dtype=torch.float64, device=device)
     if pg:
         pg.all_reduce(e2e_t, op=pg.ReduceOp.MAX)
