@@ -174,3 +174,29 @@ def test_rank_failure_surfaces_as_error_not_hang():
     got = dict(q.get(timeout=5) for _ in range(2))
     assert got[1] == "raised"
     assert got[0].startswith("error"), got[0]
+
+
+def test_bench_timed_region_pauses_gc():
+    import gc
+
+    import bench
+    assert gc.isenabled()
+    with bench.gc_paused():
+        assert not gc.isenabled()
+    assert gc.isenabled()
+    with pytest.raises(RuntimeError):
+        with bench.gc_paused():
+            raise RuntimeError("the collector comes back on errors too")
+    assert gc.isenabled()
+
+
+def test_bench_clock_sampler_reports_missing_nvml_instead_of_failing():
+    # without a GPU driver the child sampler cannot start; the bench records
+    # why and carries on with no clock samples
+    import bench
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present: the sampler starts")
+    with bench.ClockSampler(0, period_s=0.01) as clk:
+        pass
+    out = clk.summary()
+    assert out["sm_mhz"] is None and out["error"]
