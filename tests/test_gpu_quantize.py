@@ -31,7 +31,7 @@ def _edge_rows(k):
 
 @pytest.mark.parametrize("rows,k,l,scale", [(128, 64, 1, 1.0), (200, 1024, 1, 3.0),
                                             (1, 256, 2, 0.01), (385, 4096, 1, 1e3),
-                                            (256, 7168, 1, 1.0)])
+                                            (256, 7168, 1, 1.0), (1000, 2048, 3, 0.5)])
 def test_quantize_bit_exact(rows, k, l, scale):
     g = torch.Generator().manual_seed(rows + k)
     x = torch.randn(l, rows, k, generator=g) * scale
