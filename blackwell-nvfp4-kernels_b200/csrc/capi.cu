@@ -380,6 +380,17 @@ int max_active_clusters(DeviceState* d, int slot) {
   return n;
 }
 
+// Automatic split-K only when it takes at least kMinSplitSaving 256-deep K
+// blocks off each CTA: the partial exchange and its barriers cost ~5-6 us
+// (measured, unsplit vs split, us: 256x512x1024 11.9 / 16.3, 256x512x2048
+// 13.3 / 16.7, 256x1024x4096 16.6 / 18.7, 128x2048x4096 18.1 / 19.1 (saving
+// 2-12 blocks); 1536x512x7168 22.6 / 22.3, 512x768x7168 22.5 / 22.1,
+// 128x7168x16384 49.6 / 44.6 (saving 14-32 blocks)).
+constexpr int kMinSplitSaving = 14;
+bool split_pays(int k_blocks, int splits) {
+  return k_blocks - (k_blocks + splits - 1) / splits >= kMinSplitSaving;
+}
+
 template <int kBN, int kStages, int kEpiWarps, int kAccBufs>
 int launch_dual(DeviceState* d, int slot, DualParams& p, int forced_splits, int cluster,
                 cudaStream_t stream) {
@@ -397,6 +408,7 @@ int launch_dual(DeviceState* d, int slot, DualParams& p, int forced_splits, int 
                        : (4 * p.tiles <= d->num_sms ? 4 : 2);
       for (int S = want; S >= 2; S /= 2) {
         if (p.k_blocks < 2 * S) continue;
+        if (cluster == 0 && !split_pays(p.k_blocks, S)) continue;
         const int fit = S == 4 ? max_active_clusters<kStages, 4>(d, 13)
                                : max_active_clusters<kStages, 2>(d, 12);
         if (p.tiles > fit) continue;
@@ -407,6 +419,7 @@ int launch_dual(DeviceState* d, int slot, DualParams& p, int forced_splits, int 
   }
   if (kBN == 128) {
     p.splits = choose_splits(p.tiles, p.k_blocks, d->num_sms);
+    if (cluster == 0 && !split_pays(p.k_blocks, p.splits)) p.splits = 1;
     if (forced_splits >= 1) p.splits = forced_splits < p.k_blocks ? forced_splits : p.k_blocks;
   }
   if (p.splits > 1) {
