@@ -39,9 +39,10 @@ def lib(cuda_device):
 
 
 def test_noalloc_matches_allocating_entry_point_two_calls(lib):
-    # shapes with fewer 128x128 tiles than SMs, so both calls take the
-    # split-K path whose partials live in the fixed array
-    shapes = [(128, 7168, 4096, 1), (256, 1024, 2048, 1)]
+    # shapes with under a quarter as many 128x128 tiles as SMs (16 each), so
+    # both calls split K (4 and 8 splits) and keep their partials in the
+    # fixed array, the second call finding the first call's contents there
+    shapes = [(256, 1024, 2048, 1), (128, 2048, 4096, 1)]
     for i, (m, n, k, l) in enumerate(shapes):
         d = I.generate_dual_input(m, n, k, l, seed=900 + i, device="cuda")
         _lib.check(_call(lib.nvfp4_dual_gemm, d, m, n, k, l))
