@@ -674,10 +674,10 @@ def main():
 
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    if pg:
-        pg.barrier()
-    torch.cuda.synchronize()
     with ClockSampler(local) as clk, gc_paused():
+        if pg:                                  # ranks start the timed loop together
+            pg.barrier()
+        torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("timed")
         for i in range(args.steps):
             flush.zero_()                       # evict L2 between calls (outside the events)
