@@ -21,6 +21,17 @@
 #include "quantize.cuh"
 #include "moe.cuh"
 
+// Fixed split-K scratch of the allocation-free dual GEMM entry point
+// (nvfp4_dual_gemm_noalloc): fp32 partial slots followed by one ticket
+// counter per tile.  Every GPU that loads the library holds it until exit.
+namespace nvfp4 {
+constexpr size_t kNoAllocPartialBytes = size_t(20) << 20;   // 20 MiB of fp32 partial slots
+constexpr size_t kNoAllocCounterInts = 4096;                // one ticket counter per tile
+constexpr size_t kNoAllocScratchBytes = kNoAllocPartialBytes + kNoAllocCounterInts * sizeof(int);
+}  // namespace nvfp4
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[nvfp4::kNoAllocScratchBytes];
+
 namespace nvfp4 {
 
 // Per-device status word written by the kernels' bounded waits.
@@ -84,11 +95,6 @@ long long wait_limit_cycles() {
     return x > 0 ? x : 4000000000LL;  // ~2 s at 2 GHz
   }();
   return v;
-}
-
-int env_int(const char* name, int dflt) {
-  const char* e = getenv(name);
-  return e ? atoi(e) : dflt;
 }
 
 // Tuning knobs (NVFP4_* environment variables) read in one pass over the
@@ -285,6 +291,63 @@ void reset_workspaces(DeviceState* d) {
     if (kv.second.counters) cudaMemset(kv.second.counters, 0, kv.second.counter_count * sizeof(int));
 }
 
+// Once per device, with that device current: the device address of the
+// no-alloc scratch array (host code may not use the symbol itself as a pointer).
+int noalloc_scratch(DeviceState* d, unsigned char** out) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!d->noalloc_scratch) {
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
+    if (e != cudaSuccess || !ptr)
+      return fail(NVFP4_ERR_CUDA, "no-alloc scratch address: %s", cudaGetErrorString(e));
+    d->noalloc_scratch = static_cast<unsigned char*>(ptr);
+  }
+  *out = d->noalloc_scratch;
+  return NVFP4_OK;
+}
+
+// Where a dual call's split-K scratch and tensor maps come from.  The
+// ordinary entry point grows a per-stream workspace with cudaMalloc and keeps
+// encoded descriptors in a host-side cache; the allocation-free one (`fixed`
+// set) uses the library's fixed scratch array and encodes every descriptor
+// on the stack.  Kernel and split choices are the same for both.
+struct DualAlloc {
+  unsigned char* fixed = nullptr;
+};
+
+int encode_dual_operand(const DualAlloc& al, CUtensorMap* map, const void* base, int rows, int k,
+                        int l, int box_rows) {
+  return al.fixed ? encode_operand_uncached(map, base, rows, k, l, box_rows)
+                  : encode_operand(map, base, rows, k, l, box_rows);
+}
+
+// Workspace split-K scratch for `p.tiles` tiles x `p.splits` slots of
+// `slot_bytes` each: the stream's cudaMalloc'd workspace, or the fixed array
+// (rejected when too small; its counters are zeroed on `stream` first, since
+// the array keeps whatever the previous call left there).
+int dual_scratch(DeviceState* d, const DualAlloc& al, cudaStream_t stream, size_t slot_bytes,
+                 DualParams& p) {
+  const size_t need = (size_t)p.tiles * p.splits * slot_bytes;
+  if (!al.fixed) {
+    Workspace* w = nullptr;
+    int rc = get_workspace(d, stream, need, (size_t)p.tiles, &w);
+    if (rc) return rc;
+    p.ws = w->partials;
+    p.ws_ctr = w->counters;
+    return NVFP4_OK;
+  }
+  if (need > kNoAllocPartialBytes || (size_t)p.tiles > kNoAllocCounterInts)
+    return fail(NVFP4_ERR_SHAPE,
+                "split-K needs %zu bytes of partials for %d tiles x %d splits; the fixed "
+                "no-alloc scratch holds %zu bytes and %zu tiles",
+                need, p.tiles, p.splits, kNoAllocPartialBytes, kNoAllocCounterInts);
+  p.ws = reinterpret_cast<float*>(al.fixed);
+  p.ws_ctr = reinterpret_cast<int*>(al.fixed + kNoAllocPartialBytes);
+  cudaError_t e = cudaMemsetAsync(p.ws_ctr, 0, (size_t)p.tiles * sizeof(int), stream);
+  if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "counter reset: %s", cudaGetErrorString(e));
+  return NVFP4_OK;
+}
+
 // Number of K splits for the 128-wide dual kernel.  A split costs the
 // partial-sum exchange through global memory (~5 us on B200), which measured
 // slower than leaving SMs idle once there are at least a quarter as many
@@ -393,7 +456,7 @@ bool split_pays(int k_blocks, int splits) {
 
 template <int kBN, int kStages, int kEpiWarps, int kAccBufs>
 int launch_dual(DeviceState* d, int slot, DualParams& p, int forced_splits, int cluster,
-                cudaStream_t stream) {
+                const DualAlloc& al, cudaStream_t stream) {
   using Cfg = DualCfg<kBN, kStages, kEpiWarps, kAccBufs>;
   int rc = NVFP4_OK;
   p.n_blocks = (p.n + kBN - 1) / kBN;
@@ -422,15 +485,9 @@ int launch_dual(DeviceState* d, int slot, DualParams& p, int forced_splits, int 
     if (cluster == 0 && !split_pays(p.k_blocks, p.splits)) p.splits = 1;
     if (forced_splits >= 1) p.splits = forced_splits < p.k_blocks ? forced_splits : p.k_blocks;
   }
-  if (p.splits > 1) {
-    Workspace* w = nullptr;
-    const size_t slot_bytes = (size_t)2 * kBN * kBM * sizeof(float);
-    rc = get_workspace(d, stream, (size_t)p.tiles * p.splits * slot_bytes,
-                       (size_t)p.tiles, &w);
-    if (rc) return rc;
-    p.ws = w->partials;
-    p.ws_ctr = w->counters;
-  }
+  if (p.splits > 1 &&
+      (rc = dual_scratch(d, al, stream, (size_t)2 * kBN * kBM * sizeof(float), p)))
+    return rc;
   const int units = p.tiles * p.splits;
   const int grid = units < d->num_sms ? units : d->num_sms;
   if (p.splits > 1) {
@@ -449,7 +506,7 @@ int launch_dual(DeviceState* d, int slot, DualParams& p, int forced_splits, int 
 template <int kBN, int kStages>
 int launch_dual_2sm(DeviceState* d, int slot, const void* a, const void* b1, const void* b2,
                     const void* sfa, const void* sfb1, const void* sfb2, void* c, int m, int n,
-                    int k, int l, int group_m, cudaStream_t stream) {
+                    int k, int l, int group_m, const DualAlloc& al, cudaStream_t stream) {
   using Cfg = Dual2smCfg<kBN, kStages>;
   auto kern = dual_gemm_2sm_kernel<kBN, kStages>;
   int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
@@ -471,9 +528,9 @@ int launch_dual_2sm(DeviceState* d, int slot, const void* a, const void* b1, con
   p.c_lines32 = (n % 16 == 0) && (reinterpret_cast<uintptr_t>(c) % 32 == 0);
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
-  if ((rc = encode_operand(&p.tmap_a, a, m, k, l, kBM))) return rc;
-  if ((rc = encode_operand(&p.tmap_b1, b1, n, k, l, Cfg::kBN))) return rc;
-  if ((rc = encode_operand(&p.tmap_b2, b2, n, k, l, Cfg::kBN))) return rc;
+  if ((rc = encode_dual_operand(al, &p.tmap_a, a, m, k, l, kBM))) return rc;
+  if ((rc = encode_dual_operand(al, &p.tmap_b1, b1, n, k, l, Cfg::kBN))) return rc;
+  if ((rc = encode_dual_operand(al, &p.tmap_b2, b2, n, k, l, Cfg::kBN))) return rc;
   const int pairs = p.tiles < d->num_sms / 2 ? p.tiles : d->num_sms / 2;
   return launch_gemm(kern, (unsigned)(2 * pairs), Cfg::kThreads, Cfg::kSmemBytes, stream, p, 0,
                      "dual_gemm_2sm_kernel");
@@ -563,9 +620,11 @@ int launch_moe_grouped_chunk(DeviceState* d, int slot, const void* a, int a_rows
 
 using namespace nvfp4;
 
-extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, const void* sfa,
-                               const void* sfb1, const void* sfb2, void* c, int m, int n, int k,
-                               int l, void* stream_) {
+namespace nvfp4 {
+namespace {
+
+int validate_dual(const void* a, const void* b1, const void* b2, const void* sfa,
+                  const void* sfb1, const void* sfb2, const void* c, int m, int n, int k, int l) {
   if (!a || !b1 || !b2 || !sfa || !sfb1 || !sfb2 || !c)
     return fail(NVFP4_ERR_INVALID_ARG, "null pointer argument");
   if (m < 1 || n < 1 || k < 1 || l < 1)
@@ -577,11 +636,14 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   if (!aligned16(a) || !aligned16(b1) || !aligned16(b2) || !aligned16(sfa) || !aligned16(sfb1) ||
       !aligned16(sfb2) || !aligned16(c))
     return fail(NVFP4_ERR_ALIGNMENT, "all operands must be 16-byte aligned");
-  DeviceState* d = nullptr;
-  int rc = get_device(&d);
-  if (rc) return rc;
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+  return NVFP4_OK;
+}
 
+// Kernel choice and launch of one validated dual GEMM call (both entry points).
+int run_dual(DeviceState* d, const void* a, const void* b1, const void* b2, const void* sfa,
+             const void* sfb1, const void* sfb2, void* c, int m, int n, int k, int l,
+             const DualAlloc& al, cudaStream_t stream) {
+  int rc = NVFP4_OK;
   DualParams p;
   memset(&p, 0, sizeof(p));
   p.sfa = static_cast<const uint8_t*>(sfa);
@@ -597,7 +659,6 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   p.group_m = kn.dual_group_m;
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
-
   // Kernel choice: the single-CTA kernel (128-wide tiles; cluster split-K
   // when the tiles leave SMs idle; 64-wide tiles on request), or the CTA-pair
   // kernel (NVFP4_DUAL_KERNEL=pair; 96-wide tiles with NVFP4_DUAL_BN=96),
@@ -620,20 +681,36 @@ extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, co
   if (pair) {
     if (kn.dual_bn == 96)
       return launch_dual_2sm<96, 5>(d, 3, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
-                                    kn.dual_group_m, stream);
+                                    kn.dual_group_m, al, stream);
     return launch_dual_2sm<128, 5>(d, 14, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
-                                   kn.dual_group_m, stream);
+                                   kn.dual_group_m, al, stream);
   }
   // 128-wide tiles (one fused N=256 MMA per K step), split along K when
   // there are fewer tiles than SMs; 64-wide tiles only on request.
   int bn = 128;
   if (kn.dual_bn == 64 || kn.dual_bn == 128) bn = kn.dual_bn;
-  if ((rc = encode_operand(&p.tmap_a, a, m, k, l, kBM))) return rc;
-  if ((rc = encode_operand(&p.tmap_b1, b1, n, k, l, bn))) return rc;
-  if ((rc = encode_operand(&p.tmap_b2, b2, n, k, l, bn))) return rc;
-  if (bn == 128) return launch_dual<128, 4, 8, 1>(d, 0, p, kn.dual_splits, kn.dual_cluster, stream);
-  return launch_dual<64, 5, 4, 2>(d, 1, p, kn.dual_splits, kn.dual_cluster, stream);
+  if ((rc = encode_dual_operand(al, &p.tmap_a, a, m, k, l, kBM))) return rc;
+  if ((rc = encode_dual_operand(al, &p.tmap_b1, b1, n, k, l, bn))) return rc;
+  if ((rc = encode_dual_operand(al, &p.tmap_b2, b2, n, k, l, bn))) return rc;
+  if (bn == 128)
+    return launch_dual<128, 4, 8, 1>(d, 0, p, kn.dual_splits, kn.dual_cluster, al, stream);
+  return launch_dual<64, 5, 4, 2>(d, 1, p, kn.dual_splits, kn.dual_cluster, al, stream);
 }
+
+}  // namespace
+}  // namespace nvfp4
+
+extern "C" int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, const void* sfa,
+                               const void* sfb1, const void* sfb2, void* c, int m, int n, int k,
+                               int l, void* stream_) {
+  int rc = validate_dual(a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l);
+  if (rc) return rc;
+  DeviceState* d = nullptr;
+  if ((rc = get_device(&d))) return rc;
+  return run_dual(d, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l, DualAlloc{},
+                  static_cast<cudaStream_t>(stream_));
+}
+
 
 extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, void* stream_) {
   if (!groups || num_groups < 0) return fail(NVFP4_ERR_INVALID_ARG, "bad group table");
@@ -649,7 +726,8 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
       return fail(NVFP4_ERR_INVALID_ARG, "group %d: null pointer", i);
     if (g.k % kBK != 0) return fail(NVFP4_ERR_SHAPE, "group %d: K=%d not a multiple of 256", i, g.k);
     if (g.n % 8 != 0) return fail(NVFP4_ERR_SHAPE, "group %d: N=%d not a multiple of 8", i, g.n);
-    if ((long long)g.m * g.n * g.l >= (1LL << 40))
+    if ((long long)g.m * g.n * g.l >= (1LL << 40) ||
+        (long long)(g.m > g.n ? g.m : g.n) * g.k * g.l >= (1LL << 41))
       return fail(NVFP4_ERR_SHAPE, "group %d: too large", i);
     if (!aligned16(g.a) || !aligned16(g.b) || !aligned16(g.sfa_perm) || !aligned16(g.sfb_perm) ||
         !aligned16(g.c))
@@ -926,111 +1004,22 @@ extern "C" int nvfp4_moe_combine(const void* c, int c_rows, const int* dst, cons
 // servers that reserve the whole HBM budget up front for weights and KV
 // caches and hand out no further bytes, and hosts whose memory manager owns
 // every device allocation (so a library-side cudaMalloc is forbidden or
-// would fragment its pool).  Instead of the per-stream workspace that
-// nvfp4_dual_gemm grows with cudaMalloc, the split-K partials of this entry
-// point live in the fixed array below, which every GPU that loads the
-// library keeps until the process exits.
+// would fragment its pool).  The kernel and split choices are those of
+// nvfp4_dual_gemm; only a workspace split-K keeps its partial sums somewhere
+// else: in the fixed array g_noalloc_scratch (declared at the top of this
+// file) instead of the per-stream workspace that nvfp4_dual_gemm grows with
+// cudaMalloc.  Tensor maps are encoded on the stack (the descriptor cache
+// would allocate host memory).
 // ---------------------------------------------------------------------------
-namespace nvfp4 {
-namespace {
-constexpr size_t kNoAllocPartialBytes = size_t(20) << 20;   // 20 MiB of fp32 partial slots
-constexpr size_t kNoAllocCounterInts = 4096;                // one ticket counter per tile
-constexpr size_t kNoAllocScratchBytes = kNoAllocPartialBytes + kNoAllocCounterInts * sizeof(int);
-}  // namespace
-}  // namespace nvfp4
-
-static __device__ __align__(256) unsigned char g_noalloc_scratch[nvfp4::kNoAllocScratchBytes];
-
-namespace nvfp4 {
-namespace {
-
-// Once per device, with that device current: the device address of the
-// scratch array (host code may not use the symbol itself as a pointer).
-int noalloc_scratch(DeviceState* d, unsigned char** out) {
-  std::lock_guard<std::mutex> lk(g_mu);
-  if (!d->noalloc_scratch) {
-    void* ptr = nullptr;
-    cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
-    if (e != cudaSuccess || !ptr)
-      return fail(NVFP4_ERR_CUDA, "no-alloc scratch address: %s", cudaGetErrorString(e));
-    d->noalloc_scratch = static_cast<unsigned char*>(ptr);
-  }
-  *out = d->noalloc_scratch;
-  return NVFP4_OK;
-}
-
-}  // namespace
-}  // namespace nvfp4
-
 extern "C" int nvfp4_dual_gemm_noalloc(const void* a, const void* b1, const void* b2,
                                        const void* sfa, const void* sfb1, const void* sfb2,
                                        void* c, int m, int n, int k, int l, void* stream_) {
-  if (!a || !b1 || !b2 || !sfa || !sfb1 || !sfb2 || !c)
-    return fail(NVFP4_ERR_INVALID_ARG, "null pointer argument");
-  if (m < 1 || n < 1 || k < 1 || l < 1)
-    return fail(NVFP4_ERR_INVALID_ARG, "sizes must be positive (m=%d n=%d k=%d l=%d)", m, n, k, l);
-  if (k % kBK != 0) return fail(NVFP4_ERR_SHAPE, "K=%d is not a multiple of 256", k);
-  if (n % 8 != 0) return fail(NVFP4_ERR_SHAPE, "N=%d is not a multiple of 8", n);
-  if ((long long)m * n * l >= (1LL << 40) || (long long)(m > n ? m : n) * k * l >= (1LL << 41))
-    return fail(NVFP4_ERR_SHAPE, "problem too large");
-  if (!aligned16(a) || !aligned16(b1) || !aligned16(b2) || !aligned16(sfa) || !aligned16(sfb1) ||
-      !aligned16(sfb2) || !aligned16(c))
-    return fail(NVFP4_ERR_ALIGNMENT, "all operands must be 16-byte aligned");
-  DeviceState* d = nullptr;
-  int rc = get_device(&d);
+  int rc = validate_dual(a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l);
   if (rc) return rc;
-  unsigned char* scratch = nullptr;
-  if ((rc = noalloc_scratch(d, &scratch))) return rc;
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_);
-
-  constexpr int kBN = 128, kStages = 4, kEpiWarps = 8;
-  using Cfg = DualCfg<kBN, kStages, kEpiWarps, 1>;
-  DualParams p;
-  memset(&p, 0, sizeof(p));
-  p.sfa = static_cast<const uint8_t*>(sfa);
-  p.sfb1 = static_cast<const uint8_t*>(sfb1);
-  p.sfb2 = static_cast<const uint8_t*>(sfb2);
-  p.c = static_cast<__half*>(c);
-  p.m = m, p.n = n, p.k = k, p.l = l;
-  p.c_lines32 = (n % 16 == 0) && (reinterpret_cast<uintptr_t>(c) % 32 == 0);
-  p.m_blocks = (m + kBM - 1) / kBM;
-  p.n_blocks = (n + kBN - 1) / kBN;
-  p.k_blocks = k / kBK;
-  p.tiles = l * p.m_blocks * p.n_blocks;
-  p.group_m = env_int("NVFP4_DUAL_GROUP_M", 32);
-  if (p.group_m < 1) p.group_m = 1;
-  p.splits = choose_splits(p.tiles, p.k_blocks, d->num_sms);
-  const int forced = env_int("NVFP4_DUAL_SPLITS", 0);
-  if (forced >= 1) p.splits = forced < p.k_blocks ? forced : p.k_blocks;
-  p.status = d->status;
-  p.wait_limit = wait_limit_cycles();
-  if (p.splits > 1) {
-    const size_t need = (size_t)p.tiles * p.splits * 2 * kBN * kBM * sizeof(float);
-    if (need > kNoAllocPartialBytes || (size_t)p.tiles > kNoAllocCounterInts)
-      return fail(NVFP4_ERR_SHAPE,
-                  "split-K needs %zu bytes of partials for %d tiles x %d splits; the fixed "
-                  "no-alloc scratch holds %zu bytes and %zu tiles",
-                  need, p.tiles, p.splits, kNoAllocPartialBytes, kNoAllocCounterInts);
-    p.ws = reinterpret_cast<float*>(scratch);
-    p.ws_ctr = reinterpret_cast<int*>(scratch + kNoAllocPartialBytes);
-    // the array keeps the previous call's contents: the tickets must start at zero
-    cudaError_t e = cudaMemsetAsync(p.ws_ctr, 0, (size_t)p.tiles * sizeof(int), stream);
-    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "counter reset: %s", cudaGetErrorString(e));
-  }
-  // descriptors are encoded on the stack every call (the cache would allocate host memory)
-  if ((rc = encode_operand_uncached(&p.tmap_a, a, m, k, l, kBM))) return rc;
-  if ((rc = encode_operand_uncached(&p.tmap_b1, b1, n, k, l, kBN))) return rc;
-  if ((rc = encode_operand_uncached(&p.tmap_b2, b2, n, k, l, kBN))) return rc;
-  const int units = p.tiles * p.splits;
-  const int grid = units < d->num_sms ? units : d->num_sms;
-  if (p.splits > 1) {
-    auto kern = dual_gemm_kernel<kBN, kStages, kEpiWarps, 1, true>;
-    if ((rc = set_smem_once(d, 20, kern, Cfg::kSmemBytes))) return rc;
-    kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
-  } else {
-    auto kern = dual_gemm_kernel<kBN, kStages, kEpiWarps, 1, false>;
-    if ((rc = set_smem_once(d, 21, kern, Cfg::kSmemBytes))) return rc;
-    kern<<<grid, Cfg::kThreads, Cfg::kSmemBytes, stream>>>(p);
-  }
-  return check_launch("dual_gemm_kernel (no-alloc)");
+  DeviceState* d = nullptr;
+  if ((rc = get_device(&d))) return rc;
+  DualAlloc al;
+  if ((rc = noalloc_scratch(d, &al.fixed))) return rc;
+  return run_dual(d, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l, al,
+                  static_cast<cudaStream_t>(stream_));
 }

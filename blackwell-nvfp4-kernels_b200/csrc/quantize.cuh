@@ -12,9 +12,14 @@
 //   value = e2m1_rne(x / scale)  (the IEEE fp32 quotient; ties to the even code; saturating
 //                                 at 6; a value rounding to zero keeps its sign)
 //
-// The quotient is formed without a division: with r = RN(1/s),
+// The quotient is formed without a division, by Markstein's method (P.
+// Markstein, IBM J. Res. Dev. 34(1), 1990; "IA-64 and Elementary Functions",
+// 2000): a quotient estimate from a correctly rounded reciprocal, refined by
+// one fused multiply-add correction step.  With r = RN(1/s),
 //   q0 = RN(x * r),  q1 = RN(q0 + RN(x - q0 * s) * r)   (two FMAs)
-// equals RN(x / s) for every fp32 x and every e4m3 scale s (s has one of 8
+// Markstein's theorem gives RN(x / s) under conditions on the operands; here
+// the equality is proven by exhaustion instead: q1 equals RN(x / s) for every
+// fp32 x and every e4m3 scale s (s has one of 8
 // mantissas; scaling x or s by a power of two scales every step exactly, so
 // the exhaustive check over all 2^23 mantissas of x times the 8 mantissas of
 // s covers all normal operands; tests/test_formats.py repeats it).  The

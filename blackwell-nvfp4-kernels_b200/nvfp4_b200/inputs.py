@@ -130,6 +130,85 @@ def group_config_input(cfg: int, device="cuda", quantize_on=None, m_sizes=None):
 
 
 # ---------------------------------------------------------------------------
+# the reference's own inputs
+# ---------------------------------------------------------------------------
+def _atom_image(fill: torch.Tensor, sf: torch.Tensor) -> torch.Tensor:
+    """Permuted scale tensor whose padding holds `fill`: fill is the uint8
+    atom image [l, ceil(mn/128), ceil(sf_k/4), 32, 4, 4] the reference starts
+    from, sf the [mn, sf_k, l] scales written over it (row r = 128*mm + 32*mm4
+    + mm32, block j = 4*kk + kk4 go to image index (l, mm, kk, mm32, mm4, kk4))."""
+    mn, sf_k, l = sf.shape
+    rm, rk = fill.shape[1], fill.shape[2]
+    mat = fill.permute(0, 1, 4, 3, 2, 5).reshape(l, rm * 128, rk * 4).clone()
+    mat[:, :mn, :sf_k] = sf.view(torch.uint8).permute(2, 0, 1)
+    return swizzle_sf(mat.permute(1, 2, 0))
+
+
+def reference_dual_input(m: int, n: int, k: int, l: int, seed: int, device="cuda"):
+    """The dual-GEMM 10-tuple of nvfp4_dual_gemm/reference.py:80-196 for
+    (m, n, k, l, seed), made by the same torch RNG calls in the same order
+    (torch.manual_seed, then on `device`: randint of A, B1, B2 (:116, :125-127),
+    randn of C (:134), rand of the three scale tensors (:145)), so on a GPU these
+    are the reference's own inputs.  The padding of the permuted scale
+    tensors, uninitialised memory in the reference (:165), is zero here; no
+    kernel reads it for a stored output row."""
+    torch.manual_seed(seed)
+    dev = torch.device(device)
+    sf_k = ceil_div(k, SF_VEC)
+
+    def operand(mn):
+        codes = torch.randint(255, size=(l, mn, k // 2), dtype=torch.uint8, device=dev)
+        return (codes & 0b1011_1011).permute(1, 2, 0).view(torch.float4_e2m1fn_x2)
+
+    a, b1, b2 = operand(m), operand(n), operand(n)
+    c = torch.randn((l, m, n), dtype=torch.float16, device=dev).permute(1, 2, 0)
+
+    def scales(mn):
+        sf = torch.rand((l, mn, sf_k), dtype=torch.float32, device=dev) \
+            .to(dtype=torch.float8_e4m3fn).permute(1, 2, 0)
+        fill = torch.zeros((l, ceil_div(mn, 128), ceil_div(sf_k, 4), 32, 4, 4),
+                           dtype=torch.uint8, device=dev)
+        return sf, _atom_image(fill, sf)
+
+    (sfa, pa), (sfb1, pb1), (sfb2, pb2) = scales(m), scales(n), scales(n)
+    return (a, b1, b2, sfa, sfb1, sfb2, pa, pb1, pb2, c)
+
+
+def reference_group_input(m, n, k, g: int, seed: int, device="cuda"):
+    """The grouped-GEMM 4-tuple of nvfp4_group_gemm/reference.py:126-196 for
+    (m, n, k, g, seed), made by the same torch RNG calls in the same order
+    (torch.manual_seed, then per group: randint of A and B and randn of C on
+    `device` (:168-179), randint of the plain scales on the CPU generator
+    (:182-187), and for each permuted scale tensor a randint of its whole
+    image on `device` that supplies the padding (:97)), so on a GPU these are
+    the reference's own inputs.  The plain scales stay on the CPU, as there."""
+    torch.manual_seed(seed)
+    dev = torch.device(device)
+    abc, sfab, sfab_perm, sizes = [], [], [], []
+    for i in range(g):
+        mi, ni, ki = m[i], n[i], k[i]
+        sf_k = ceil_div(ki, SF_VEC)
+        a = torch.randint(-1, 2, (1, mi, ki // 2), dtype=torch.int8, device=dev).permute(1, 2, 0)
+        b = torch.randint(-1, 2, (1, ni, ki // 2), dtype=torch.int8, device=dev).permute(1, 2, 0)
+        c = torch.randn((1, mi, ni), dtype=torch.float16, device=dev).permute(1, 2, 0)
+        sfa = torch.randint(1, 3, (1, mi, sf_k), dtype=torch.int8) \
+            .to(dtype=torch.float8_e4m3fn).permute(1, 2, 0)
+        sfb = torch.randint(1, 3, (1, ni, sf_k), dtype=torch.int8) \
+            .to(dtype=torch.float8_e4m3fn).permute(1, 2, 0)
+
+        def permuted(mn, sf):
+            fill = torch.randint(1, 3, (1, ceil_div(mn, 128), ceil_div(sf_k, 4), 32, 4, 4),
+                                 dtype=torch.int8, device=dev).to(dtype=torch.float8_e4m3fn)
+            return _atom_image(fill.view(torch.uint8), sf.to(dev))
+
+        abc.append((a.view(torch.float4_e2m1fn_x2), b.view(torch.float4_e2m1fn_x2), c))
+        sfab.append((sfa, sfb))
+        sfab_perm.append((permuted(mi, sfa), permuted(ni, sfb)))
+        sizes.append((mi, ni, ki, 1))
+    return abc, sfab, sfab_perm, sizes
+
+
+# ---------------------------------------------------------------------------
 # reference-task distributions
 # ---------------------------------------------------------------------------
 def _ref_fp4_bytes(l, mn, k, g, mode):

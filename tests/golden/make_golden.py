@@ -14,13 +14,25 @@ reference's ``ref_kernel`` does (nvfp4_dual_gemm/reference.py:50-76,
 nvfp4_group_gemm/reference.py:56-72) on small seeded inputs and stores inputs
 and outputs -> ``scaled_mm_golden.npz``.
 
-    python tests/golden/make_golden.py --reference /path/to/reference   # part 1
-    python tests/golden/make_golden.py --gpu --out gpurun_out/           # part 2
+Part 3 (CPU, needs the reference checkout): runs the reference's own
+``generate_input`` (nvfp4_dual_gemm/reference.py:80-196,
+nvfp4_group_gemm/reference.py:126-196) with every ``device="cuda"`` it names
+redirected to the CPU, and records a SHA-256 digest of each tensor it returns
+-> ``reference_inputs_golden.json``.  ``nvfp4_b200.inputs.reference_dual_input``
+/ ``reference_group_input`` restate those generators call for call; run on the
+CPU they must reproduce the digests, which shows they make the same RNG calls
+in the same order (on a GPU both then draw from the CUDA generator).
+
+    python tests/golden/make_golden.py --reference /path/to/reference   # parts 1 and 3
+    python tests/golden/make_golden.py --gpu --out <out-dir>/           # part 2
 """
 from __future__ import annotations
 
 import argparse
+import contextlib
+import hashlib
 import importlib.util
+import json
 import sys
 from pathlib import Path
 
@@ -126,6 +138,104 @@ def make_scaled_mm(out_dir: Path):
     print("wrote", out_dir / "scaled_mm_golden.npz")
 
 
+# (m, n, k, l, seed) / (m list, n list, k list, g, seed): ragged rows, L = 2,
+# a K that leaves a partial 4-block column of scale atoms, the task seeds
+DUAL_INPUT_CASES = [(128, 256, 256, 1, 1111), (256, 384, 512, 2, 1153), (100, 136, 320, 1, 1195)]
+GROUP_INPUT_CASES = [([96, 128], [128, 256], [256, 512], 2, 1111),
+                     ([40, 56, 200], [512, 384, 136], [256, 320, 512], 3, 1153)]
+
+
+def _u8(t: torch.Tensor) -> torch.Tensor:
+    """Logical-order bytes (same shape for 1-byte types, flat otherwise)."""
+    t = t.cpu()
+    if t.element_size() == 1:
+        return t.view(torch.uint8).contiguous()
+    return t.contiguous().reshape(-1).view(torch.uint8)
+
+
+def _digest(t: torch.Tensor) -> str:
+    return hashlib.sha256(_u8(t).numpy().tobytes()).hexdigest()
+
+
+def _valid_scales(perm: torch.Tensor, mn: int, sf_k: int) -> torch.Tensor:
+    """[mn, sf_k, l] scales read back out of a permuted [32,4,rm,4,rk,l] tensor."""
+    r = torch.arange(mn)[:, None]
+    j = torch.arange(sf_k)[None, :]
+    u = _u8(perm)
+    return u[r % 32, (r % 128) // 32, r // 128, j % 4, j // 4, :]
+
+
+def input_digests(kind: str, data) -> dict:
+    """Digests of every tensor of a task tuple.  Dual permuted scale tensors
+    are digested over their written entries only: the reference leaves their
+    padding uninitialised."""
+    if kind == "dual":
+        names = ["a", "b1", "b2", "sfa", "sfb1", "sfb2", "sfa_perm", "sfb1_perm", "sfb2_perm", "c"]
+        out = {}
+        for i, (name, t) in enumerate(zip(names, data)):
+            if name.endswith("_perm"):
+                plain = data[i - 3]
+                t = _valid_scales(t, plain.shape[0], plain.shape[1])
+            out[name] = _digest(t)
+        return out
+    abc, sfab, perm, sizes = data
+    out = {"sizes": [list(s) for s in sizes]}
+    for g, ((a, b, c), (sa, sb), (pa, pb)) in enumerate(zip(abc, sfab, perm)):
+        for name, t in (("a", a), ("b", b), ("c", c), ("sfa", sa), ("sfb", sb),
+                        ("sfa_perm", pa), ("sfb_perm", pb)):
+            out[f"{name}_{g}"] = _digest(t)
+    return out
+
+
+@contextlib.contextmanager
+def cuda_redirected_to_cpu():
+    """Every tensor a function asks for on "cuda" is made on the CPU instead
+    (factory calls with device=..., .cuda(), .to("cuda"))."""
+    def redirect(kw):
+        d = kw.get("device")
+        if d is not None and torch.device(d).type == "cuda":
+            kw["device"] = "cpu"
+        return kw
+
+    saved = {}
+    for name in ("randint", "randn", "rand", "empty", "arange", "zeros"):
+        saved[name] = getattr(torch, name)
+        setattr(torch, name, lambda *a, _f=saved[name], **kw: _f(*a, **redirect(kw)))
+    to0, cuda0 = torch.Tensor.to, torch.Tensor.cuda
+
+    def to(self, *a, **kw):
+        if a and isinstance(a[0], (str, torch.device)) and torch.device(a[0]).type == "cuda":
+            return self
+        return to0(self, *a, **kw)
+
+    torch.Tensor.to = to
+    torch.Tensor.cuda = lambda self, *a, **kw: self
+    try:
+        yield
+    finally:
+        for name, f in saved.items():
+            setattr(torch, name, f)
+        torch.Tensor.to, torch.Tensor.cuda = to0, cuda0
+
+
+def make_reference_inputs(ref_root: Path):
+    dual = _load_reference_module(ref_root, "nvfp4_dual_gemm")
+    grp = _load_reference_module(ref_root, "nvfp4_group_gemm")
+    out = {"dual": [], "group": []}
+    with cuda_redirected_to_cpu():
+        for case in DUAL_INPUT_CASES:
+            out["dual"].append({"case": list(case),
+                                "digests": input_digests("dual", dual.generate_input(*case))})
+        for case in GROUP_INPUT_CASES:
+            out["group"].append({"case": [list(case[0]), list(case[1]), list(case[2]), case[3],
+                                          case[4]],
+                                 "digests": input_digests("group", grp.generate_input(*case))})
+    out["torch"] = torch.__version__
+    path = HERE / "reference_inputs_golden.json"
+    path.write_text(json.dumps(out, indent=1) + "\n")
+    print("wrote", path)
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", type=Path, default=None)
@@ -135,5 +245,6 @@ if __name__ == "__main__":
     if args.gpu:
         make_scaled_mm(args.out)
     else:
-        assert args.reference is not None, "--reference <checkout> is required for part 1"
+        assert args.reference is not None, "--reference <checkout> is required for parts 1, 3"
         make_swizzle(args.reference)
+        make_reference_inputs(args.reference)

@@ -80,6 +80,21 @@ def test_grouped_rejects_bad_arguments_without_gpu(lib):
     assert lib.nvfp4_grouped_gemm(t, 1, None) == _lib.NVFP4_OK
 
 
+def test_grouped_rejects_operands_beyond_the_descriptor_range_without_gpu(lib):
+    # M*N*L is small, but max(M, N)*K*L = 2^41 bytes-worth of K elements: the
+    # same bound the dual entry point applies before encoding tensor maps
+    t = (_lib.Group * 1)()
+    t[0] = _lib.Group(4096, 4096, 4096, 4096, 4096, 1 << 20, 8, 1 << 21, 1)
+    assert lib.nvfp4_grouped_gemm(t, 1, None) == _lib.NVFP4_ERR_SHAPE
+    assert b"too large" in lib.nvfp4_last_error()
+    t[0] = _lib.Group(4096, 4096, 4096, 4096, 4096, 8, 1 << 19, 1 << 20, 4)
+    assert lib.nvfp4_grouped_gemm(t, 1, None) == _lib.NVFP4_ERR_SHAPE
+    # same for the allocation-free dual entry point, which shares the dual validation
+    p = ctypes.c_void_p(4096)
+    assert lib.nvfp4_dual_gemm_noalloc(p, p, p, p, p, p, p, 1 << 20, 8, 1 << 21, 1, None) == \
+        _lib.NVFP4_ERR_SHAPE
+
+
 def test_quantize_rejects_bad_arguments_without_gpu(lib):
     p = ctypes.c_void_p(4096)
     f = lib.nvfp4_quantize

@@ -116,6 +116,21 @@ def test_dual_both_tile_widths(m, n, k, l, bn, monkeypatch):
     assert_close(run_dual(data), oracle_dual(data), f"dual bn={bn} {m}x{n}x{k}x{l}")
 
 
+@pytest.mark.parametrize("m,n,k,l", DUAL_TASK_BENCH)
+def test_dual_benchmark_shapes_automatic_choice(m, n, k, l):
+    """The timed benchmark shapes with no knob set: the automatic kernel and
+    split choice (CTA pair for the 256-row shapes, unsplit otherwise)."""
+    data = I.generate_dual_input(m, n, k, l, seed=2024 + m, device="cuda")
+    assert_close(run_dual(data), oracle_dual(data), f"dual automatic {m}x{n}x{k}")
+
+
+def test_dual_config2_full_output():
+    """Configuration 2 (M=128, N=7168, K=16384; cluster split-K) in full:
+    every one of the 128 x 7168 outputs against the oracle."""
+    data = I.dual_config_input(2, device="cuda")
+    assert_close(run_dual(data), oracle_dual(data), "dual cfg2 full output")
+
+
 @pytest.mark.parametrize("splits", [2, 3, 5, 16])
 @pytest.mark.parametrize("m,n,k,l", [(256, 512, 4096, 1), (200, 264, 2048, 1), (384, 640, 1024, 2),
                                      (128, 7168, 4096, 1)])

@@ -3,16 +3,19 @@
 Some callers cannot let a library allocate device memory while they run:
 serving engines that hand the entire HBM budget to weights and KV caches
 before the first request, and hosts whose own memory manager must own every
-device byte.  For them the C ABI offers nvfp4_dual_gemm_noalloc, which keeps
-its split-K partial sums in a fixed array inside the library instead of a
-workspace grown with cudaMalloc.  These tests call it through the C ABI and
-check it against the ordinary entry point, nvfp4_dual_gemm, on two calls in a
-row (the array is shared by every call and keeps the previous call's
-contents), within the tolerance the parity tests use.  This file is named to
-be collected last.
-"""
-import ctypes
+device byte.  For them the C ABI offers nvfp4_dual_gemm_noalloc.  It makes
+the same kernel and split choices as nvfp4_dual_gemm, but a K split that
+exchanges partial sums through global memory keeps them in a fixed array
+inside the library instead of a workspace grown with cudaMalloc.
 
+These tests call it through the C ABI, twice in a row per shape (the array is
+shared by every call and keeps the previous call's contents), and check each
+result against the CPU oracle within the tolerance the parity tests use, and
+bit for bit against the ordinary entry point.  The shapes cover each branch of
+the kernel choice: a K split through the fixed array, an unsplit call, a
+cluster K split (partials exchanged between CTAs, no array) and the CTA-pair
+kernel.  This file is named to be collected last.
+"""
 import numpy as np
 import pytest
 import torch
@@ -25,11 +28,25 @@ from oracle import nvfp4_oracle as O
 pytestmark = pytest.mark.gpu
 RTOL = ATOL = 1e-2
 
+# (m, n, k, l, branch) -- the branch nvfp4_dual_gemm takes on a 148-SM B200
+SHAPES = [
+    (128, 2048, 4096, 1, "K split into 8 through the fixed array"),
+    (128, 1024, 4608, 1, "K split into 9 through the fixed array"),
+    (512, 4096, 1024, 1, "unsplit"),
+    (256, 1024, 8192, 1, "cluster K split (4 CTAs)"),
+    (256, 3072, 4096, 1, "CTA pair"),
+]
+
 
 def _call(fn, d, m, n, k, l):
     stream = torch.cuda.current_stream().cuda_stream
     return fn(d[0].data_ptr(), d[1].data_ptr(), d[2].data_ptr(), d[6].data_ptr(),
               d[7].data_ptr(), d[8].data_ptr(), d[9].data_ptr(), m, n, k, l, stream)
+
+
+def _oracle(d):
+    u8 = lambda t: t.detach().cpu().view(torch.uint8).numpy()
+    return O.ref_dual_batched(*(u8(t) for t in d[:6]))
 
 
 @pytest.fixture(scope="module")
@@ -38,21 +55,24 @@ def lib(cuda_device):
     return _lib.load()
 
 
-def test_noalloc_matches_allocating_entry_point_two_calls(lib):
-    # shapes with under a quarter as many 128x128 tiles as SMs (16 each), so
-    # both calls split K (4 and 8 splits) and keep their partials in the
-    # fixed array, the second call finding the first call's contents there
-    shapes = [(256, 1024, 2048, 1), (128, 2048, 4096, 1)]
-    for i, (m, n, k, l) in enumerate(shapes):
-        d = I.generate_dual_input(m, n, k, l, seed=900 + i, device="cuda")
-        _lib.check(_call(lib.nvfp4_dual_gemm, d, m, n, k, l))
-        assert _lib.device_status() == 0
-        want = d[9].clone()
-        d[9].zero_()
+@pytest.mark.parametrize("m,n,k,l,branch", SHAPES, ids=[s[4] for s in SHAPES])
+def test_noalloc_matches_oracle_two_calls(lib, m, n, k, l, branch):
+    d = I.generate_dual_input(m, n, k, l, seed=900 + m + n, device="cuda")
+    want = _oracle(d)
+    outs = []
+    for call in range(2):
+        d[9].fill_(float("nan"))
         _lib.check(_call(lib.nvfp4_dual_gemm_noalloc, d, m, n, k, l))
         assert _lib.device_status() == 0
-        bad, idx = O.allclose_report(d[9].cpu().numpy(), want.cpu().numpy(), RTOL, ATOL)
-        assert bad == 0, f"call {i} ({m}x{n}x{k}): {bad} mismatches, first {idx[:3]}"
+        got = d[9].cpu().numpy()
+        bad, idx = O.allclose_report(got, want, RTOL, ATOL)
+        assert bad == 0, f"{branch}, call {call}: {bad} mismatches, first {idx[:3]}"
+        outs.append(d[9].clone())
+    # the same kernels in the same order as the allocating entry point
+    d[9].zero_()
+    _lib.check(_call(lib.nvfp4_dual_gemm, d, m, n, k, l))
+    assert _lib.device_status() == 0
+    assert torch.equal(outs[0], outs[1]) and torch.equal(outs[0], d[9])
 
 
 def test_noalloc_rejects_shapes_beyond_its_scratch(lib, monkeypatch):
