@@ -1,26 +1,43 @@
-"""Benchmark of the NVFP4 hot paths on B200; prints ONE JSON line (rank 0).
+"""Benchmark of the NVFP4 hot paths on B200; the last JSON line (rank 0) is the headline.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W]            # the default suite
+    python bench.py --config C [--impl ours|reference]              # one configuration
     python bench.py --suite task     # the reference's task.yml shapes vs its published geomeans
 
-Default workload: configuration 1 (dual GEMM M=8192 N=14336 K=4096, the
-compute-bound SiLU-gated FFN shape).  A step is one dual-GEMM call over one
-batch of synthetic inputs (seeded N(0,1) operands quantised to NVFP4).
+Default suite, one JSON line each, headline last:
+  N = 1: configurations 2, 3 and 4, the task.yml benchmark geomeans (dual and
+         grouped), then configuration 1 (dual GEMM M=8192 N=14336 K=4096, the
+         compute-bound SiLU-gated FFN shape) -- the headline.
+  N > 1: configurations 2 and 4 (strong scaling), configuration 1 weak-scaled
+         (an extra, labelled line), then configuration 1 strong-scaled -- the
+         headline.
+A step is one call of the hot path over one batch of synthetic input (seeded
+N(0,1) operands quantised to NVFP4).
 
 * value: device time of the K timed calls (CUDA events on the launching
-  stream, L2 flushed between calls outside the events), max over ranks;
-  whole-job effective TFLOP/s = all ranks' FLOP / that time.
+  stream; L2 flushed between calls outside the events by a 512 MiB write
+  followed by a 512 MiB read, so no dirty flush lines are written back inside
+  the next call), max over ranks; whole-job effective TFLOP/s = the FLOP all
+  ranks did / that time.
+* sustained (headline): the same calls back to back for at least 2 s of
+  kernel time, with the SM clock sampled over them; both figures also as
+  cycles per call (us x median SM MHz).
 * e2e: the same metric through the public drop-in ``custom_kernel`` with the
   step's inputs copied from pinned host memory and the output copied back,
   inside the timed region.
 * roofline: dominant kernel's achieved FLOP/s (or GB/s) against the NVFP4
   dense peak (4x the measured bf16 peak) or the measured HBM copy bandwidth.
 * cpu_baseline / --impl reference: the CPU oracle (dequantise + fp32 matmul,
-  the reference's ref_kernel restated) on a bounded sample of the workload.
+  the reference's ref_kernel restated), timed by one protocol for both arms
+  in a spawned process that holds no CUDA context: W warm-up steps, then K
+  steps, each a 2048 x 2048 output block (all of K) of the configuration,
+  with every BLAS thread of the host; plus configuration 0 in full.
 
-Multi-GPU (torchrun, one rank per GPU): dual GEMM is sharded along N with the
-per-rank shard fixed at the configuration's N (weak scaling, no collective on
-the data path); grouped configurations assign experts by LPT (strong scaling).
+Multi-GPU (torchrun, one rank per GPU, no collective on the data path): the
+dual GEMM is sharded along N in contiguous 128-row shards of the
+configuration's N (shard.n_shard: strong scaling; the rank shards
+concatenated are the single-GPU problem); grouped configurations assign
+experts by LPT (strong scaling).
 """
 from __future__ import annotations
 
@@ -62,27 +79,50 @@ def gc_paused():
 L2_FLUSH_BYTES = 512 << 20
 
 
+class L2Flush:
+    """Evicts L2 between timed calls: a write over one 512 MiB buffer, then a
+    read over another.  The read pass evicts the written lines (their
+    write-back happens here, not inside the next timed call) and leaves L2
+    holding clean lines of a buffer no kernel reads."""
+
+    def __init__(self, device):
+        self.w = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+        self.r = torch.zeros(L2_FLUSH_BYTES // 4, dtype=torch.int32, device=device)
+        self.sink = torch.empty((), dtype=torch.int32, device=device)
+
+    def __call__(self):
+        self.w.zero_()
+        torch.amax(self.r, dim=0, out=self.sink)
+
+    describe = "flushed (512 MiB write + 512 MiB read) between timed calls"
+
+
 # ---------------------------------------------------------------------------
 # workload
 # ---------------------------------------------------------------------------
-def dual_workload(cfg: int, rank: int, world: int, device):
-    """Rank's dual GEMM: A replicated (same seed everywhere), B1/B2 = this
-    rank's N-shard of a global N = N_cfg * world (weak scaling)."""
+def dual_workload(cfg: int, rank: int, world: int, device, scaling: str = "strong"):
+    """Rank's share of dual configuration `cfg`, A replicated (same seed
+    everywhere).  strong: B1/B2 rows [n0, n1) = shard.n_shard(N, world, rank)
+    of the configuration's own operands, so the rank outputs side by side are
+    the single-GPU C; weak: every rank a full-N problem (rank 0's is the
+    single-GPU configuration, the others draw their own B1/B2)."""
     from nvfp4_b200 import inputs as I
+    from nvfp4_b200.shard import n_shard
     spec = I.DUAL_CONFIGS[cfg]
     m, n, k = spec["m"], spec["n"], spec["k"]
-    ga = torch.Generator().manual_seed(spec["seed"])
-    a = torch.randn(m, k, generator=ga)
-    gb = torch.Generator().manual_seed(spec["seed"] * 1000 + rank)
-    if rank == 0:   # rank 0's shard is exactly the single-GPU configuration
-        gb = torch.Generator().manual_seed(spec["seed"])
-        torch.randn(m, k, generator=gb)
-    b1 = torch.randn(n, k, generator=gb)
-    b2 = torch.randn(n, k, generator=gb)
-    data = I.dual_from_fp32(a, b1, b2, device=device)
-    flop = 4.0 * m * n * k
-    nbytes = m * k // 2 + 2 * n * k // 2 + (m + 2 * n) * k // 16 + 2 * m * n
-    desc = dict(workload=f"dual_gemm_cfg{cfg}", m=m, n_per_rank=n, n_global=n * world, k=k, l=1)
+    g = torch.Generator().manual_seed(spec["seed"])
+    a = torch.randn(m, k, generator=g)
+    if scaling == "weak" and rank > 0:
+        g = torch.Generator().manual_seed(spec["seed"] * 1000 + rank)
+    b1 = torch.randn(n, k, generator=g)
+    b2 = torch.randn(n, k, generator=g)
+    n0, n1 = n_shard(n, world, rank) if scaling == "strong" else (0, n)
+    data = I.dual_from_fp32(a, b1[n0:n1], b2[n0:n1], device=device)
+    nr = n1 - n0
+    flop = 4.0 * m * nr * k
+    nbytes = m * k // 2 + 2 * nr * k // 2 + (m + 2 * nr) * k // 16 + 2 * m * nr
+    desc = dict(workload=f"dual_gemm_cfg{cfg}", m=m, n_global=n if scaling == "strong" else n * world,
+                n_this_rank=nr, n_rows_this_rank=[n0, n1], k=k, l=1)
     return data, flop, nbytes, desc
 
 
@@ -202,14 +242,14 @@ def shape_workload(args, device):
         dict(workload=f"grouped_gemm_{'+'.join(map(str, ms))}x{n}x{k}", groups=ms, n=n, k=k)
 
 
-def make_workload(cfg, rank, world, device, tokens=32768):
+def make_workload(cfg, rank, world, device, tokens=32768, scaling="strong"):
     if cfg == 5:
         return quant_workload(rank, world, device)
     if cfg == 6:
         return moe_workload(rank, world, device, tokens)
     if cfg == 7:
         return moe_layer_workload(rank, world, device, tokens)
-    return dual_workload(cfg, rank, world, device) if cfg in (0, 1, 2) else \
+    return dual_workload(cfg, rank, world, device, scaling) if cfg in (0, 1, 2) else \
         group_workload(cfg, rank, world, device)
 
 
@@ -357,44 +397,82 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # CPU oracle timing
 # ---------------------------------------------------------------------------
-def cpu_sample_step(cfg, data_cpu, rows, cols):
-    """One bounded sample of the workload through the oracle: `rows` output
-    rows x `cols` output columns (dual) or the same block of one group."""
+CPU_SAMPLE = 2048   # output rows and columns of one CPU oracle step (all of K)
+
+
+def _cpu_step(cfg: int, rows: int = CPU_SAMPLE, cols: int = CPU_SAMPLE):
+    """(step function, FLOP per step, description) of one CPU oracle step of
+    configuration `cfg`: a rows x cols output block over the configuration's
+    whole K, seeded N(0,1) operands quantised to NVFP4 on the host
+    (the dual GEMM: both GEMMs and the SiLU gate; grouped: one group's GEMM,
+    as many rows as the largest group has, at most `rows`)."""
+    from nvfp4_b200 import inputs as I
+    from nvfp4_b200.formats import quantize_nvfp4
     from oracle import nvfp4_oracle as O
+    g = torch.Generator().manual_seed(100 + cfg)
     if cfg in (0, 1, 2):
-        a, b1, b2, sfa, sfb1, sfb2 = data_cpu
-        O.ref_dual(a[:rows], b1[:cols], b2[:cols], sfa[:rows], sfb1[:cols], sfb2[:cols])
-        return 4.0 * rows * cols * a.shape[1] * 2
-    a, b, sfa, sfb = data_cpu
-    O.ref_group(a[:rows], b[:cols], sfa[:rows], sfb[:cols])
-    return 2.0 * rows * cols * a.shape[1] * 2
+        spec = I.DUAL_CONFIGS[cfg]
+        k = spec["k"]
+        rows, cols = min(rows, spec["m"]), min(cols, spec["n"])
+        (a, sa), (b1, s1), (b2, s2) = (
+            [t.numpy() for t in quantize_nvfp4(torch.randn(r, k, generator=g))]
+            for r in (rows, cols, cols))
+        return (lambda: O.ref_dual(a, b1, b2, sa, s1, s2)), 4.0 * rows * cols * k, \
+            f"oracle ref_dual on a {rows}x{cols} output block x K={k}"
+    spec = I.GROUP_CONFIGS[cfg]
+    ms = I.config3_m_sizes(spec["seed"], spec["groups"]) if cfg == 3 else \
+        I.config4_m_sizes(spec["seed"], spec["experts"], spec["tokens"], spec["zipf_s"])
+    k = spec["k"]
+    rows, cols = min(rows, max(ms)), min(cols, spec["n"])
+    (a, sa), (b, sb) = ([t.numpy() for t in quantize_nvfp4(torch.randn(r, k, generator=g))]
+                        for r in (rows, cols))
+    return (lambda: O.ref_group(a, b, sa, sb)), 2.0 * rows * cols * k, \
+        f"oracle ref_group on a {rows}x{cols} output block x K={k}"
 
 
-def cpu_inputs(cfg, data):
-    u8 = lambda t: t.detach().cpu().view(torch.uint8).numpy()[:, :, 0]
-    if cfg in (0, 1, 2):
-        return [u8(t) for t in data[:6]]
-    abc, sfab, _, sizes = data
-    i = max(range(len(sizes)), key=lambda j: sizes[j][0])   # largest group
-    return [u8(abc[i][0]), u8(abc[i][1]), u8(sfab[i][0]), u8(sfab[i][1])]
+def cpu_oracle_protocol(cfg: int, steps: int, warmup: int) -> dict:
+    """The CPU baseline of both bench arms: `warmup` untimed then `steps` timed
+    oracle steps of configuration `cfg` (each a 2048 x 2048 block, all of K),
+    plus configuration 0 in full (256 x 512 x 1024, repeated for >= 2 s), with
+    the BLAS pool at every host thread.  Runs in a spawned child process
+    (cpu_oracle_in_child) so neither arm's CUDA context, pinned buffers or
+    clock sampler shares the host with it."""
+    from threadpoolctl import threadpool_limits
+    cores = cpu_cores()
+    torch.set_num_threads(cores)
+    with threadpool_limits(limits=cores):
+        step, flop, sample = _cpu_step(cfg)
+        for _ in range(warmup):
+            step()
+        secs = 0.0
+        for _ in range(steps):
+            t0 = time.perf_counter()
+            step()
+            secs += time.perf_counter() - t0
+        step0, flop0, _ = _cpu_step(0, 256, 512)
+        step0()
+        reps0, secs0 = 0, 0.0
+        while reps0 < 3 or secs0 < 2.0:
+            t0 = time.perf_counter()
+            step0()
+            secs0 += time.perf_counter() - t0
+            reps0 += 1
+    return {"value": round(flop * steps / secs / 1e12, 5), "unit": "TFLOP/s", "cores": cores,
+            "kind": "port", "steps": steps, "warmup": warmup,
+            "ms_per_step": round(secs * 1e3 / steps, 2),
+            "sample": f"{sample} per step (bounded sample, not extrapolated to the full "
+                      f"configuration: TFLOP/s of the block itself), numpy + BLAS on {cores} "
+                      f"threads, spawned process without a CUDA context",
+            "full_config0": {"value": round(flop0 * reps0 / secs0 / 1e12, 5), "unit": "TFLOP/s",
+                             "reps": reps0, "ms_per_call": round(secs0 * 1e3 / reps0, 3),
+                             "sample": "configuration 0 in full (256x512x1024 dual GEMM), "
+                                       "no extrapolation"}}
 
 
-def cpu_sample_shape(cfg, data_cpu):
-    rows = min(data_cpu[0].shape[0], 2048)
-    cols = min(data_cpu[1].shape[0], 2048)
-    return rows, cols
-
-
-def time_cpu(cfg, data_cpu, budget_s: float, min_reps: int = 1):
-    rows, cols = cpu_sample_shape(cfg, data_cpu)
-    cpu_sample_step(cfg, data_cpu, min(rows, 64), min(cols, 64))     # warm caches / threads
-    flops, secs, reps = 0.0, 0.0, 0
-    while reps < min_reps or secs < budget_s:
-        t0 = time.perf_counter()
-        flops += cpu_sample_step(cfg, data_cpu, rows, cols)
-        secs += time.perf_counter() - t0
-        reps += 1
-    return flops / secs / 1e12, reps, rows, cols
+def cpu_oracle_in_child(cfg: int, steps: int, warmup: int) -> dict:
+    import multiprocessing as mp
+    with mp.get_context("spawn").Pool(1) as pool:
+        return pool.apply(cpu_oracle_protocol, (cfg, steps, warmup))
 
 
 def time_cpu_quant(x_dev, budget_s: float):
@@ -525,18 +603,20 @@ TASK_INPUTS = 15        # distinct inputs per shape, as the reference's eval.py 
 
 
 def task_inputs(kind, shape, device):
-    """The 15 inputs eval.py builds per benchmark (seed += 42 before each)."""
+    """The 15 inputs eval.py builds per benchmark (seed += 42 before each),
+    made on the device by the restated reference generators: the reference
+    harness's own tensors for these seeds."""
     from nvfp4_b200 import inputs as I
     out = []
     for i in range(TASK_INPUTS):
         seed = TASK_SEED + 42 * (i + 1)
         if kind == "dual":
             m, n, k = shape
-            out.append(I.generate_dual_input(m, n, k, 1, seed, device=device))
+            out.append(I.reference_dual_input(m, n, k, 1, seed, device=device))
         else:
             ms, n, k = shape
-            out.append(I.generate_group_input(ms, [n] * len(ms), [k] * len(ms), len(ms), seed,
-                                              device=device))
+            out.append(I.reference_group_input(ms, [n] * len(ms), [k] * len(ms), len(ms), seed,
+                                               device=device))
     return out
 
 
@@ -548,20 +628,19 @@ def task_flop(kind, shape):
     return sum(2.0 * m * n * k for m in ms)
 
 
-def run_task_suite(args):
+def task_suite_lines(args, device):
     """Per reference benchmark shape: L2 flushed, then the 15 distinct inputs
     run back to back between two CUDA events; the per-call mean of `steps`
-    such batches.  One JSON line per task: geomean us against the published
+    such batches.  One result per task: geomean us against the published
     geomean of the reference's best submission."""
     from nvfp4_b200 import _lib
     from nvfp4_b200.dual_gemm import custom_kernel as dual_kernel
     from nvfp4_b200.group_gemm import custom_kernel as group_kernel
-    torch.cuda.set_device(0)
-    device = torch.device("cuda", 0)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    flush = L2Flush(device)
+    lines = []
     for kind, shapes, fn in (("dual", TASK_DUAL, dual_kernel), ("group", TASK_GROUP, group_kernel)):
         per_shape, per_shape_std, tflops = [], [], []
-        with ClockSampler(0, period_s=0.02) as clk:
+        with ClockSampler(device.index, period_s=0.02) as clk:
             for shape in shapes:
                 datas = task_inputs(kind, shape, device)
                 for _ in range(args.warmup):
@@ -571,7 +650,7 @@ def run_task_suite(args):
                 times = []
                 with gc_paused():
                     for _ in range(args.steps):
-                        flush.zero_()
+                        flush()
                         e0 = torch.cuda.Event(enable_timing=True)
                         e1 = torch.cuda.Event(enable_timing=True)
                         e0.record()
@@ -588,17 +667,24 @@ def run_task_suite(args):
         assert _lib.device_status() == 0
         geo = float(np.exp(np.mean(np.log(per_shape))))
         pub = TASK_PUBLISHED_US[kind]
-        print(json.dumps({
+        lines.append({
             "metric": f"runtime geomean over the reference's task.yml benchmark shapes "
                       f"({'dual' if kind == 'dual' else 'grouped'} GEMM)",
             "value": round(geo, 3), "unit": "us", "higher_is_better": False,
             "vs_baseline": round(geo / pub, 4), "reference_published_us": pub,
             "per_shape_us": per_shape, "per_shape_std_us": per_shape_std, "per_shape_tflops": tflops,
             "shapes": [list(s) if kind == "dual" else [s[0], s[1], s[2]] for s in shapes],
-            "method": f"{TASK_INPUTS} distinct seeded inputs per shape (reference generator "
-                      f"distributions), L2 flushed before each batch, mean per call over "
-                      f"{args.steps} batches, custom_kernel API",
-            "n_gpus": 1, "clocks": clk.summary()}), flush=True)
+            "method": f"{TASK_INPUTS} distinct inputs per shape (the reference generator's own "
+                      f"tensors, seeds {TASK_SEED}+42i), L2 flushed before each batch, mean per "
+                      f"call over {args.steps} batches, custom_kernel API",
+            "n_gpus": 1, "clocks": clk.summary()})
+    return lines
+
+
+def run_task_suite(args):
+    torch.cuda.set_device(0)
+    for line in task_suite_lines(args, torch.device("cuda", 0)):
+        print(json.dumps(line), flush=True)
 
 
 def metric_name(cfg):
@@ -612,117 +698,157 @@ def metric_name(cfg):
         "NVFP4 effective TFLOPS (grouped GEMM)"
 
 
-def main():
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=50)
-    ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--config", type=int, default=1, choices=[0, 1, 2, 3, 4, 5, 6, 7],
-                    help="0-4: BASELINE configurations; 5: device quantisation of config 1's "
-                         "operands; 6: MoE dispatch of config 4's routing; 7: the MoE expert "
-                         "layer around config 4")
-    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--e2e-steps", type=int, default=5)
-    ap.add_argument("--cpu-budget", type=float, default=12.0)
-    ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--kernel-only", action="store_true",
-                    help="device-timed calls only (no e2e, no CPU baseline): the profiling run")
-    ap.add_argument("--suite", default=None, choices=["task"],
-                    help="task: the reference's own task.yml benchmark shapes, one line per task")
-    ap.add_argument("--shape", default=None,
-                    help="M,N,K: kernel-only dual GEMM at this size (profiling runs)")
-    ap.add_argument("--tokens", type=int, default=32768,
-                    help="configuration 6: tokens to dispatch (32768 = configuration 4's routing)")
-    ap.add_argument("--group-shape", default=None,
-                    help="M1:M2:...,N,K: kernel-only grouped GEMM at these sizes (profiling runs)")
-    args = ap.parse_args()
-    if args.shape or args.group_shape:
-        args.kernel_only = True
-    assert args.warmup >= 3 or args.impl == "reference", "need >= 3 warm-up steps"
+def scaling_of(cfg: int, dual_scaling: str) -> str:
+    if cfg in (0, 1, 2):
+        return dual_scaling
+    return "weak" if cfg in (6, 7) else "strong"
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    cfg = args.config
 
-    if args.impl == "reference":
-        return run_reference_arm(args, cfg, rank, world)
-    if args.suite == "task":
-        return run_task_suite(args)
+def timed_calls(cfg, data, calls, flush, stream):
+    """Per-call device ms of `calls` calls, L2 flushed before each (outside
+    the events), CUDA events on the launching stream."""
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(calls)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(calls)]
+    for i in range(calls):
+        flush()
+        starts[i].record(stream)
+        call(cfg, data)
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
 
-    torch.cuda.set_device(local)
-    device = torch.device("cuda", local)
-    pg = None
-    if world > 1:
-        import datetime
-        import torch.distributed as dist
-        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
-        pg = dist
 
+def all_max(pg, device, v: float) -> float:
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return t.item()
+
+
+def all_sum(pg, device, v: float) -> float:
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.SUM)
+    return t.item()
+
+
+def run_config(cfg, args, rank, world, device, pg, flush, *, dual_scaling="strong", e2e=True,
+               sustained=False, cpu_baseline=False):
+    """One configuration: warm-up, K timed calls, optionally the sustained
+    loop, the end-to-end leg and the CPU baseline.  Returns rank 0's JSON
+    line as a dict (every rank takes the same collective steps)."""
     from nvfp4_b200 import _lib
-    if args.shape or args.group_shape:
-        cfg, data, flop, nbytes, desc = shape_workload(args, device)
-    else:
-        data, flop, nbytes, desc = make_workload(cfg, rank, world, device, args.tokens)
+    data, flop, nbytes, desc = make_workload(cfg, rank, world, device, args.tokens, dual_scaling)
     stream = torch.cuda.current_stream(device)
-    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
-
     for _ in range(args.warmup):
         call(cfg, data)
     torch.cuda.synchronize()
     assert _lib.device_status() == 0
 
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    with ClockSampler(local) as clk, gc_paused():
+    with ClockSampler(device.index) as clk, gc_paused():
         if pg:                                  # ranks start the timed loop together
             pg.barrier()
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("timed")
-        for i in range(args.steps):
-            flush.zero_()                       # evict L2 between calls (outside the events)
-            starts[i].record(stream)
-            call(cfg, data)
-            ends[i].record(stream)
-        torch.cuda.synchronize()
+        per_call_ms = timed_calls(cfg, data, args.steps, flush, stream)
         torch.cuda.nvtx.range_pop()
     if pg:
         pg.barrier()
     status = _lib.device_status()
     assert status == 0, f"device status {status:#x}"
-    per_call_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
-    t_total = torch.tensor([sum(per_call_ms)], dtype=torch.float64, device=device)
-    flop_t = torch.tensor([flop], dtype=torch.float64, device=device)
-    if pg:
-        pg.all_reduce(t_total, op=pg.ReduceOp.MAX)
-        pg.all_reduce(flop_t, op=pg.ReduceOp.SUM)
-    t_max_s = t_total.item() / 1e3
-    total_flop = flop_t.item() * args.steps
+    t_max_s = all_max(pg, device, sum(per_call_ms)) / 1e3
+    flop_all = all_sum(pg, device, flop)
+    bytes_all = all_sum(pg, device, float(nbytes))
     ms_per_step = t_max_s * 1e3 / args.steps
-    if cfg in (5, 6):   # bytes-moved metric for the quantiser and the dispatch
-        bytes_t = torch.tensor([float(nbytes)], dtype=torch.float64, device=device)
-        if pg:
-            pg.all_reduce(bytes_t, op=pg.ReduceOp.SUM)
-        value = bytes_t.item() * args.steps / t_max_s / 1e9
+    quant = cfg in (5, 6)        # bytes-moved metric for the quantiser and the dispatch
+    unit = "GB/s" if quant else "TFLOP/s"
+    value = bytes_all * args.steps / t_max_s / 1e9 if quant else flop_all * args.steps / t_max_s / 1e12
+    clocks = clk.summary()
+    scaling = scaling_of(cfg, dual_scaling)
+    par = ("n-shard" if cfg in (0, 1, 2) and dual_scaling == "strong" else
+           "n-replica" if cfg in (0, 1, 2) else "token-shard" if cfg in (6, 7) else
+           "expert-lpt") + str(world)
+    result = {
+        "metric": metric_name(cfg), "value": round(value, 2), "unit": unit,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms_per_step, 5), "us_per_call": round(ms_per_step * 1e3, 2),
+        "us_per_call_std": round(statistics.stdev(per_call_ms) * 1e3, 2) if len(per_call_ms) > 1 else 0.0,
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+        "dtype": ("int32 routing + fp32 -> e2m1 + e4m3 block16" if cfg == 6 else
+                  "fp32 -> e2m1 + e4m3 block16") if quant
+        else "fp32 tokens -> nvfp4 x nvfp4 -> fp32 acc -> fp16 -> fp32 combine" if cfg == 7
+        else "nvfp4(e2m1+e4m3 block16) x nvfp4 -> fp32 acc -> fp16",
+        "data": "synthetic: seeded N(0,1) fp32 quantised to NVFP4",
+        "config": {**desc, "parallelism": par, "l2": L2Flush.describe},
+    }
+    if clocks.get("sm_mhz"):
+        result["cycles_per_call"] = round(ms_per_step * 1e3 * clocks["sm_mhz"])
+
+    if sustained:
+        # back to back for >= args.sustain_s of kernel time (same calls on every rank)
+        calls = max(args.steps, int(args.sustain_s * 1e3 / ms_per_step) + 1)
+        with ClockSampler(device.index, period_s=0.02) as sclk, gc_paused():
+            if pg:
+                pg.barrier()
+            torch.cuda.synchronize()
+            sus_ms = timed_calls(cfg, data, calls, flush, stream)
+        assert _lib.device_status() == 0
+        ts = all_max(pg, device, sum(sus_ms)) / 1e3
+        sc = sclk.summary()
+        sus = {"value": round(flop_all * calls / ts / 1e12, 2), "unit": unit, "calls": calls,
+               "kernel_seconds": round(ts, 3), "us_per_call": round(ts * 1e6 / calls, 2),
+               "clocks": sc}
+        if sc.get("sm_mhz"):
+            sus["cycles_per_call"] = round(ts * 1e6 / calls * sc["sm_mhz"])
+        result["sustained"] = sus
+
+    if e2e:
+        result["e2e"] = e2e_leg(cfg, data, args, device, stream, pg, flop_all, bytes_all)
+
+    # ---- roofline of the dominant kernel (the GEMM kernel is the only launch)
+    hbm_peak, bf16_peak, peak_kind = load_peaks()
+    nvfp4_peak = 4.0 * bf16_peak
+    avg_launch_s = statistics.mean(per_call_ms) / 1e3
+    hbm_bound = cfg in (2, 5, 6)
+    if hbm_bound:
+        ach = nbytes / avg_launch_s / 1e9
+        roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                "frac": round(ach / hbm_peak, 4)}
     else:
-        value = total_flop / t_max_s / 1e12
+        ach = flop / avg_launch_s / 1e12
+        roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": nvfp4_peak,
+                "unit": "TFLOP/s", "frac": round(ach / nvfp4_peak, 4)}
+    roof["traffic"] = load_traffic(desc["workload"]) if world == 1 else None
+    roof["algorithmic_bytes"] = nbytes
+    roof["peak_source"] = (f"{peak_kind}: NVFP4 dense = 4 x bf16 {bf16_peak} TFLOP/s"
+                           if not hbm_bound else f"{peak_kind}: HBM copy {hbm_peak} GB/s")
+    if world > 1:
+        roof["note"] = "per rank (rank 0's launches)"
+    result["roofline"] = roof
+    launches = 4 if cfg == 6 else 6 if cfg == 7 else len(data) if quant else 1
+    result["gpu_launches"] = args.steps * launches
+    result["clocks"] = clocks
 
-    if args.kernel_only:
-        if rank == 0:
-            print(json.dumps({"metric": metric_name(cfg), "value": round(value, 2),
-                              "unit": "GB/s" if cfg in (5, 6) else "TFLOP/s",
-                              "us_per_call": round(ms_per_step * 1e3, 2),
-                              "config": desc, "kernel_only": True, "clocks": clk.summary()}),
-                  flush=True)
-        if pg:
-            pg.destroy_process_group()
-        return
+    if cpu_baseline and rank == 0 and world == 1 and not args.no_cpu_baseline:
+        if cfg == 6:
+            result["cpu_baseline"] = time_cpu_moe(data[0], data[1], data[2], args.cpu_budget)
+        elif cfg == 7:
+            result["cpu_baseline"] = time_cpu_moe_layer(data, args.cpu_budget)
+        elif quant:
+            result["cpu_baseline"] = time_cpu_quant(data[0][0], args.cpu_budget)
+        else:
+            result["cpu_baseline"] = cpu_oracle_in_child(cfg, args.steps, args.warmup)
+    del data
+    torch.cuda.empty_cache()
+    return result
 
-    # ---- e2e through the public API with pinned host buffers.  Every step
-    # uploads its inputs and reads its result back; the upload of step i+1
-    # runs on its own stream while step i's result is read back on another
-    # (PCIe is full duplex), and a step's compute waits for its inputs and
-    # for the previous read-back (the outputs are reused).
+
+def e2e_leg(cfg, data, args, device, stream, pg, flop_all, bytes_all):
+    """The metric through the public API with pinned host buffers.  Every step
+    uploads its inputs and reads its result back; the upload of step i+1 runs
+    on its own stream while step i's result is read back on another (PCIe is
+    full duplex), and a step's compute waits for its inputs and for the
+    previous read-back (the outputs are reused)."""
     ins, outs = device_tensors(cfg, data)
     h_ins = [t.detach().cpu().pin_memory() for t in ins]
     h_outs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outs]
@@ -761,134 +887,141 @@ def main():
         stream.wait_event(done_out)
         ee.record(stream)
         torch.cuda.synchronize()
-    e2e_t = torch.tensor([es.elapsed_time(ee) / 1e3], dtype=torch.float64, device=device)
-    if pg:
-        pg.all_reduce(e2e_t, op=pg.ReduceOp.MAX)
+    t = all_max(pg, device, es.elapsed_time(ee) / 1e3)
     quant = cfg in (5, 6)
-    if quant:   # bytes-moved metric for the quantiser and the dispatch
-        e2e_value = bytes_t.item() * args.e2e_steps / e2e_t.item() / 1e9
-    else:
-        e2e_value = flop_t.item() * args.e2e_steps / e2e_t.item() / 1e12
-    unit = "GB/s" if quant else "TFLOP/s"
+    v = (bytes_all * args.e2e_steps / t / 1e9) if quant else (flop_all * args.e2e_steps / t / 1e12)
+    del h_ins, h_outs
+    return {"value": round(v, 3), "unit": "GB/s" if quant else "TFLOP/s", "h2d_bytes_per_step": h2d,
+            "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
+            "api": "nvfp4_b200 public API (ctypes -> libnvfp4_b200.so)",
+            "copies": "pinned host; step i+1's upload overlaps step i's read-back"}
 
-    # ---- roofline of the dominant kernel (the GEMM kernel is the only launch)
-    hbm_peak, bf16_peak, peak_kind = load_peaks()
-    nvfp4_peak = 4.0 * bf16_peak
-    avg_launch_s = statistics.mean(per_call_ms) / 1e3
-    hbm_bound = cfg in (2, 5, 6)
-    traffic = load_traffic(desc["workload"])
-    if hbm_bound:
-        ach = nbytes / avg_launch_s / 1e9
-        roof = {"bound": "hbm", "achieved": round(ach, 1), "peak": hbm_peak, "unit": "GB/s",
-                "frac": round(ach / hbm_peak, 4)}
-    else:
-        ach = flop / avg_launch_s / 1e12
-        roof = {"bound": "tensor", "achieved": round(ach, 1), "peak": nvfp4_peak,
-                "unit": "TFLOP/s", "frac": round(ach / nvfp4_peak, 4)}
-    roof["traffic"] = traffic
-    roof["algorithmic_bytes"] = nbytes
-    roof["peak_source"] = (f"{peak_kind}: NVFP4 dense = 4 x bf16 {bf16_peak} TFLOP/s"
-                           if not hbm_bound else f"{peak_kind}: HBM copy {hbm_peak} GB/s")
 
-    result = {
-        "metric": metric_name(cfg), "value": round(value, 2), "unit": unit,
-        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(ms_per_step, 5), "us_per_call": round(ms_per_step * 1e3, 2),
-        "us_per_call_std": round(statistics.stdev(per_call_ms) * 1e3, 2) if len(per_call_ms) > 1 else 0.0,
-        "higher_is_better": True, "scaling": "weak" if cfg in (0, 1, 2, 6, 7) else "strong",
-        "vs_baseline": None,
-        "dtype": ("int32 routing + fp32 -> e2m1 + e4m3 block16" if cfg == 6 else
-                  "fp32 -> e2m1 + e4m3 block16") if quant
-        else "fp32 tokens -> nvfp4 x nvfp4 -> fp32 acc -> fp16 -> fp32 combine" if cfg == 7
-        else "nvfp4(e2m1+e4m3 block16) x nvfp4 -> fp32 acc -> fp16",
-        "data": "synthetic: seeded N(0,1) fp32 quantised to NVFP4",
-        "config": {**desc, "parallelism": f"{'n-shard' if cfg in (0, 1, 2) else 'token-shard' if cfg in (6, 7) else 'expert-lpt'}{world}",
-                   "l2": f"flushed ({L2_FLUSH_BYTES >> 20} MiB write) between timed calls"},
-        "e2e": {"value": round(e2e_value, 3), "unit": unit, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
-                "api": "nvfp4_b200 public API (ctypes -> libnvfp4_b200.so)",
-                "copies": "pinned host; step i+1's upload overlaps step i's read-back"},
-        "roofline": roof,
-        "gpu_launches": args.steps * (4 if cfg == 6 else 6 if cfg == 7 else len(data) if quant else 1),
-        "clocks": clk.summary(),
-    }
+def shape_run(args, device):
+    """--shape / --group-shape: device-timed calls of one ad-hoc size (profiling runs)."""
+    cfg, data, flop, nbytes, desc = shape_workload(args, device)
+    flush = L2Flush(device)
+    for _ in range(args.warmup):
+        call(cfg, data)
+    torch.cuda.synchronize()
+    with ClockSampler(device.index) as clk, gc_paused():
+        ms = timed_calls(cfg, data, args.steps, flush, torch.cuda.current_stream(device))
+    us = statistics.mean(ms) * 1e3
+    print(json.dumps({"metric": metric_name(cfg), "value": round(flop / us / 1e6, 2),
+                      "unit": "TFLOP/s", "us_per_call": round(us, 2),
+                      "hbm_gbs": round(nbytes / us / 1e3, 1), "config": desc,
+                      "kernel_only": True, "clocks": clk.summary()}), flush=True)
 
-    if rank == 0 and world == 1 and not args.no_cpu_baseline and cfg == 6:
-        result["cpu_baseline"] = time_cpu_moe(data[0], data[1], data[2], args.cpu_budget)
-    elif rank == 0 and world == 1 and not args.no_cpu_baseline and cfg == 7:
-        result["cpu_baseline"] = time_cpu_moe_layer(data, args.cpu_budget)
-    elif rank == 0 and world == 1 and not args.no_cpu_baseline and quant:
-        result["cpu_baseline"] = time_cpu_quant(data[0][0], args.cpu_budget)
-    elif rank == 0 and world == 1 and not args.no_cpu_baseline:
-        dc = cpu_inputs(cfg, data)
-        torch.set_num_threads(cpu_cores())
-        v, reps, rows, cols = time_cpu(cfg, dc, args.cpu_budget)
-        result["cpu_baseline"] = {
-            "value": round(v, 5), "unit": "TFLOP/s", "cores": cpu_cores(), "kind": "port",
-            "sample": f"oracle ref ({'dual' if cfg < 3 else 'group'}) on a {rows}x{cols} output "
-                      f"block x K={dc[0].shape[1] * 2}, {reps} reps (~{args.cpu_budget:.0f} s)"}
-    if pg:
-        pg.barrier()
-        pg.destroy_process_group()
-    if rank == 0:
-        print(json.dumps(result), flush=True)
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=None, choices=[0, 1, 2, 3, 4, 5, 6, 7],
+                    help="one configuration only (default: the suite, headline configuration 1). "
+                         "0-4: BASELINE configurations; 5: device quantisation of config 1's "
+                         "operands; 6: MoE dispatch of config 4's routing; 7: the MoE expert "
+                         "layer around config 4")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="dual configurations with --config: N split over the ranks (strong) or "
+                         "a full-N problem per rank (weak)")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--sustain-s", type=float, default=2.0,
+                    help="seconds of back-to-back kernel time in the headline's sustained figure")
+    ap.add_argument("--cpu-budget", type=float, default=12.0,
+                    help="seconds of CPU work for the configuration 5-7 baselines")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--kernel-only", action="store_true",
+                    help="device-timed calls only (no e2e, no CPU baseline): the profiling run")
+    ap.add_argument("--suite", default=None, choices=["task"],
+                    help="task: the reference's own task.yml benchmark shapes, one line per task")
+    ap.add_argument("--shape", default=None,
+                    help="M,N,K: kernel-only dual GEMM at this size (profiling runs)")
+    ap.add_argument("--tokens", type=int, default=32768,
+                    help="configuration 6: tokens to dispatch (32768 = configuration 4's routing)")
+    ap.add_argument("--group-shape", default=None,
+                    help="M1:M2:...,N,K: kernel-only grouped GEMM at these sizes (profiling runs)")
+    args = ap.parse_args()
+    assert args.warmup >= 3 or args.impl == "reference", "need >= 3 warm-up steps"
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return run_reference_arm(args, 1 if args.config is None else args.config, rank, world)
+    if args.suite == "task":
+        return run_task_suite(args)
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if args.shape or args.group_shape:
+        return shape_run(args, device)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=300))
+        pg = dist
+    flush = L2Flush(device)
+    full = not args.kernel_only
+
+    def emit(line):
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+
+    ok = False
+    try:
+        if args.config is not None:
+            emit(run_config(args.config, args, rank, world, device, pg, flush,
+                            dual_scaling=args.scaling, e2e=full, sustained=full and args.config == 1,
+                            cpu_baseline=full))
+            ok = True
+            return
+        # the default suite: supporting lines first, the headline last
+        for c in ((2, 3, 4) if world == 1 else (2, 4)):
+            emit(run_config(c, args, rank, world, device, pg, flush, e2e=full))
+        if world == 1:
+            for line in task_suite_lines(args, device):
+                emit(line)
+        else:
+            line = run_config(1, args, rank, world, device, pg, flush, dual_scaling="weak", e2e=False)
+            line["note"] = "extra line: weak scaling (every rank a full-N problem); not the headline"
+            emit(line)
+        emit(run_config(1, args, rank, world, device, pg, flush, dual_scaling="strong", e2e=full,
+                        sustained=full, cpu_baseline=full))
+        ok = True
+    finally:
+        if pg:
+            if ok:
+                pg.barrier()
+            pg.destroy_process_group()
 
 
 def run_reference_arm(args, cfg, rank, world):
     """The reference's CPU path (its ref_kernel restated as the numpy oracle)
-    on the host cores: rank 0 only; other ranks exit without work."""
+    on the host cores: rank 0 only; other ranks exit without work.  The
+    dual / grouped configurations use cpu_oracle_protocol, the same protocol
+    as the GPU arm's cpu_baseline."""
     if rank != 0:
         return
-    from nvfp4_b200 import inputs as I
     if cfg in (5, 6):
         return run_reference_bytes_arm(args, cfg, world)
     if cfg == 7:
         return run_reference_layer_arm(args, world)
-    if cfg in (0, 1, 2):
-        spec = I.DUAL_CONFIGS[cfg]
-        g = torch.Generator().manual_seed(spec["seed"])
-        rows, cols = min(spec["m"], 2048), min(spec["n"], 2048)
-        k = spec["k"]
-        a = torch.randn(spec["m"], k, generator=g)[:rows]
-        b1 = torch.randn(spec["n"], k, generator=g)[:cols]
-        b2 = torch.randn(spec["n"], k, generator=g)[:cols]
-        d = I.dual_from_fp32(a, b1, b2, device="cpu")
-        dc = [t.view(torch.uint8).numpy()[:, :, 0] for t in d[:6]]
-        wl = f"dual_gemm_cfg{cfg}"
-    else:
-        d = I.group_config_input(cfg, device="cpu") if cfg == 3 else None
-        if d is None:   # config 4: largest expert only
-            ms = I.config4_m_sizes()
-            spec = I.GROUP_CONFIGS[4]
-            gen = torch.Generator().manual_seed(7)
-            mbig = min(max(ms), 2048)
-            d = I.group_from_fp32([(torch.randn(mbig, spec["k"], generator=gen),
-                                    torch.randn(spec["n"], spec["k"], generator=gen))], device="cpu")
-        dc = cpu_inputs(cfg, d)
-        wl = f"grouped_gemm_cfg{cfg}"
-    torch.set_num_threads(cpu_cores())
-    rows, cols = cpu_sample_shape(cfg, dc)
-    for _ in range(args.warmup):
-        cpu_sample_step(cfg, dc, rows, cols)
-    budget = max(0.0, 150.0 / max(1, args.steps))
-    flops, secs = 0.0, 0.0
-    for _ in range(args.steps):
-        t0 = time.perf_counter()
-        flops += cpu_sample_step(cfg, dc, rows, cols)
-        secs += time.perf_counter() - t0
-    v = flops / secs / 1e12
-    sample = (f"numpy oracle (dequantise + fp32 matmul) on a {rows}x{cols} output block "
-              f"x K={dc[0].shape[1] * 2} per step")
+    r = cpu_oracle_in_child(cfg, args.steps, args.warmup)
+    wl = f"dual_gemm_cfg{cfg}" if cfg in (0, 1, 2) else f"grouped_gemm_cfg{cfg}"
     print(json.dumps({
-        "impl": "reference", "metric": metric_name(cfg), "value": round(v, 5), "unit": "TFLOP/s",
+        "impl": "reference", "metric": metric_name(cfg), "value": r["value"], "unit": "TFLOP/s",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(secs * 1e3 / args.steps, 3), "higher_is_better": True,
-        "scaling": "weak" if cfg in (0, 1, 2) else "strong", "vs_baseline": None,
+        "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+        "scaling": scaling_of(cfg, "strong"), "vs_baseline": None,
         "dtype": "fp32 (dequantised nvfp4)", "data": "synthetic: seeded N(0,1) quantised to NVFP4",
-        "config": {"workload": wl, "sample_rows": rows, "sample_cols": cols, "budget_s": budget},
-        "cpu_baseline": {"value": round(v, 5), "unit": "TFLOP/s", "cores": cpu_cores(),
-                         "kind": "port", "sample": sample},
-        "e2e": {"value": round(v, 5), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+        "config": {"workload": wl, "sample": r["sample"]},
+        "cpu_baseline": r,
+        "e2e": {"value": r["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }), flush=True)
 

@@ -1,6 +1,7 @@
 """CPU: host-side logic that needs no GPU: the grouped plan cache, the
 multi-GPU partitioners, and the multi-rank timing reduction over gloo."""
 import os
+from pathlib import Path
 
 import pytest
 import torch
@@ -200,3 +201,43 @@ def test_bench_clock_sampler_reports_missing_nvml_instead_of_failing():
         pass
     out = clk.summary()
     assert out["sm_mhz"] is None and out["error"]
+
+
+def test_bench_strong_shards_concatenate_to_the_single_gpu_problem():
+    """bench.py's strong-scaled dual workload: each rank's B1/B2 rows and
+    permuted scale atoms are its contiguous 128-row slice of the single-GPU
+    configuration's operands, and A is replicated."""
+    import bench
+    one, flop1, _, _ = bench.dual_workload(0, 0, 1, "cpu", "strong")
+    u8 = lambda t: t.view(torch.uint8)
+    for world in (2, 4):
+        flops = 0.0
+        for rank in range(world):
+            d, flop, _, desc = bench.dual_workload(0, rank, world, "cpu", "strong")
+            n0, n1 = desc["n_rows_this_rank"]
+            assert desc["n_global"] == 512 and n1 - n0 == desc["n_this_rank"]
+            assert torch.equal(u8(d[0]), u8(one[0]))
+            for i in (1, 2):
+                assert torch.equal(u8(d[i]), u8(one[i])[n0:n1])
+                assert torch.equal(u8(d[i + 6]), u8(one[i + 6])[:, :, n0 // 128:n1 // 128])
+            flops += flop
+        assert flops == flop1
+
+
+def test_bench_reference_arm_runs_on_the_host():
+    """--impl reference: the oracle protocol in a spawned process, one JSON
+    line with the reference-arm keys (no GPU needed)."""
+    import json
+    import subprocess
+    import sys
+    root = Path(__file__).resolve().parent.parent
+    out = subprocess.run([sys.executable, str(root / "bench.py"), "--impl", "reference",
+                          "--config", "0", "--steps", "2", "--warmup", "1"],
+                         capture_output=True, text=True, timeout=600, cwd=root)
+    assert out.returncode == 0, out.stderr[-2000:]
+    line = json.loads(out.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and line["value"] > 0
+    assert line["e2e"]["h2d_bytes_per_step"] == 0 and line["e2e"]["value"] == line["value"]
+    cb = line["cpu_baseline"]
+    assert cb["kind"] == "port" and cb["cores"] >= 1 and cb["steps"] == 2
+    assert cb["full_config0"]["value"] > 0 and "no extrapolation" in cb["full_config0"]["sample"]
