@@ -104,7 +104,7 @@ long long wait_limit_cycles() {
 struct Knobs {
   int dual_group_m = 32;   // NVFP4_DUAL_GROUP_M (measured: 16 -> 32 saves ~1.5% on 8192x14336x4096)
   int dual_splits = 0;     // NVFP4_DUAL_SPLITS (0 = automatic)
-  int dual_bn = 0;         // NVFP4_DUAL_BN (64 / 128, or 96 / 128 for the pair kernel; 0 = automatic)
+  int dual_bn = 0;         // NVFP4_DUAL_BN (64 / 128, or 64 / 96 / 128 for the pair kernel; 0 = automatic)
   int dual_kernel = 0;     // NVFP4_DUAL_KERNEL: 0 automatic, 1 pair (CTA-pair kernel), 2 single
   int dual_cluster = 0;    // NVFP4_DUAL_CLUSTER: 0 automatic, 1 off, 2 / 4 forced cluster split-K
   int grouped_bn = 0;      // NVFP4_GROUPED_BN (128 / 256; 0 = automatic)
@@ -681,6 +681,9 @@ int run_dual(DeviceState* d, const void* a, const void* b1, const void* b2, cons
   if (pair) {
     if (kn.dual_bn == 96)
       return launch_dual_2sm<96, 5>(d, 3, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
+                                    kn.dual_group_m, al, stream);
+    if (kn.dual_bn == 64)
+      return launch_dual_2sm<64, 7>(d, 15, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
                                     kn.dual_group_m, al, stream);
     return launch_dual_2sm<128, 5>(d, 14, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
                                    kn.dual_group_m, al, stream);

@@ -6,13 +6,15 @@
 // (nvfp4_dual_gemm/reference.py:27-77); own design:
 //
 // * a CTA pair (cluster of 2 on neighbouring SMs) owns a 256 x kBN tile of C
-//   (kBN = 128, or 96).  CTA r holds A rows [256*mp + 128*r, +128) and one
+//   (kBN = 128, 96 or 64).  CTA r holds A rows [256*mp + 128*r, +128) and one
 //   kBN-row B tile: CTA 0 the B1 rows of the tile's columns, CTA 1 the B2
 //   rows.  One tcgen05.mma.cta_group::2 with M = 256, N = 2*kBN per 64-deep
 //   K step then writes, in each CTA's TMEM, its 128 rows x [gate kBN | up
-//   kBN].  Per SM and K step: A 16 KB + B 16 KB of operands for 128 x kBN
+//   kBN].  Per SM and K step: A 16 KB + B kBN/8 KB of operands for 128 x kBN
 //   outputs (the single-CTA kernel: 48 KB for 128 x 128 outputs), and one
-//   MMA instruction covers both SMs;
+//   MMA instruction covers both SMs.  64-wide tiles put twice as many pairs
+//   on a shape with few 256-row blocks (e.g. M = 256, N = 4096: 128 CTAs
+//   instead of 64) at 30 KB per SM and K step;
 // * one accumulator; eight epilogue warps per CTA pull their gate and up
 //   columns into registers and release the accumulator (remote arrives on
 //   the leader's barrier) before the math and the stores;
@@ -20,11 +22,14 @@
 //   blocks covering the tile onto a landing barrier; four staging warps per
 //   CTA write them into TMEM with tcgen05.st (SFA: 4 columns per K step;
 //   SFB: column 8j + c holds B rows 32c..32c+31 of the 2*kBN-row operand,
-//   whole atom rows for 128-wide tiles, gathered 4-byte columns for 96-wide
-//   ones) and arrive on the leader's per-stage barrier.  Each pipeline stage
+//   whole atom rows for 128-wide tiles, gathered 4-byte columns for 96- and
+//   64-wide ones) and arrive on the leader's per-stage barrier.  Each pipeline stage
 //   owns one TMEM scale buffer: refilling a stage already waits for the
 //   MMAs that read it;
-// * both producers count their tile bytes on the leader's stage barrier
+// * each CTA issues its copies from two threads in parallel, one for the
+//   operand tiles and one for the scale atoms (a single thread issuing both
+//   measured ~840 cycles per K step, slower than the MMAs of a 64-wide tile);
+//   both CTAs count their tile bytes on the leader's stage barrier
 //   (TMA .cta_group::2, no multicast); the leader commits to both CTAs
 //   (tcgen05.commit multicast); cross-CTA handshakes use CTA-scope-release
 //   remote arrives; cluster barriers bracket setup and teardown.  All waits
@@ -56,21 +61,24 @@ struct Dual2smParams {
 
 template <int kBN_, int kStages>
 struct Dual2smCfg {
-  static constexpr int kBN = kBN_;                     // C columns per tile: 96 or 128
+  static constexpr int kBN = kBN_;                     // C columns per tile: 64, 96 or 128
   static constexpr int kNmma = 2 * kBN;                // pair MMA N = [B1 tile ; B2 tile]
   static constexpr int kGroups = kBN / 32;             // 32-row groups per B tile
-  static constexpr int kSfbBlocks = kBN == 128 ? 1 : 2;   // 128-row atom blocks covering a tile
+  static constexpr int kSfbBlocks = kBN == 96 ? 2 : 1;    // 128-row atom blocks covering a tile
   static constexpr int kABytes = kBM * kBK / 2;        // 16 KB
-  static constexpr int kBBytes = kBN * kBK / 2;        // 12 or 16 KB
+  static constexpr int kBBytes = kBN * kBK / 2;        // 8, 12 or 16 KB
   static constexpr int kSfaBytes = kSfStageBytes;      // 4 atoms of this CTA's A rows
   static constexpr int kSfbBytes = kSfbBlocks * kSfStageBytes;   // per B operand
-  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + 2 * kSfbBytes;   // 38 KB
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + 2 * kSfbBytes;   // 30-38 KB
   static constexpr int kPairTxBytes = 2 * (kABytes + kBBytes);
   static constexpr int kEpiWarps = 8;                   // 2 per TMEM quadrant
-  static constexpr int kColsPerWarp = kBN / 2;         // 48 or 64 columns of gate and of up
+  static constexpr int kColsPerWarp = kBN / 2;         // 32, 48 or 64 columns of gate and of up
   static constexpr int kSfWarps = 4;
+  // warp roles: epilogue [0, 8), tile producer 8, MMA 9, scale producer 10,
+  // scale staging [11, 15)
   static constexpr int kProdWarp = kEpiWarps, kMmaWarp = kEpiWarps + 1;
-  static constexpr int kThreads = 32 * (kEpiWarps + 2 + kSfWarps);
+  static constexpr int kSfProdWarp = kEpiWarps + 2, kSfWarp0 = kEpiWarps + 3;
+  static constexpr int kThreads = 32 * (kEpiWarps + 3 + kSfWarps);
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024;
   static constexpr int kTmemCols = 512;
   static constexpr int kAccBufs = 1;
@@ -79,7 +87,7 @@ struct Dual2smCfg {
   static constexpr int kSfBufCols = 48;                // per stage: SFA 4x4 + SFB 4x8 (6 used)
   static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned");
   static_assert(kSfCol + kStages * kSfBufCols <= kTmemCols, "TMEM budget: one scale buffer per stage");
-  static_assert(kBN == 96 || kBN == 128, "tile width");
+  static_assert(kBN == 64 || kBN == 96 || kBN == 128, "tile width");
 };
 
 struct PairTile2 { int l, mp, nb; };
@@ -105,7 +113,7 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
   using Cfg = Dual2smCfg<kBN, kStages>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_full[kStages], bar_empty[kStages];
-  __shared__ uint64_t bar_sf_landed[kStages], bar_sf_full[kStages];
+  __shared__ uint64_t bar_sf_landed[kStages];
   __shared__ uint64_t bar_acc_full[Cfg::kAccBufs], bar_acc_empty[Cfg::kAccBufs];
   __shared__ uint64_t bar_drain;
   __shared__ uint32_t s_tmem_base;
@@ -120,10 +128,11 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(smem_u32(&bar_full[s]), 1);
+      // the leader's expect_tx arrival + one per staging warp of both CTAs (+ the
+      // TMA bytes of both CTAs)
+      mbar_init(smem_u32(&bar_full[s]), 1 + 2 * Cfg::kSfWarps);
       mbar_init(smem_u32(&bar_empty[s]), 1);
       mbar_init(smem_u32(&bar_sf_landed[s]), 1);
-      mbar_init(smem_u32(&bar_sf_full[s]), 2 * Cfg::kSfWarps);      // both CTAs' staging warps
     }
     for (int b = 0; b < Cfg::kAccBufs; ++b) {
       mbar_init(smem_u32(&bar_acc_full[b]), 1);
@@ -150,9 +159,16 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
   const AbortCtl ctl{&s_abort, p.status, p.wait_limit};
   const int rest_k = p.k / kKStep;   // 64-deep atoms per 128-row block
 
-  if (warp == Cfg::kProdWarp) {
-    // ------------------------------------------------------------ TMA producer (both CTAs)
+  if (warp == Cfg::kProdWarp || warp == Cfg::kSfProdWarp) {
+    // ------------------------------------------------------------ TMA producers (both CTAs)
+    // Two threads issue each stage's copies in parallel: warp kProdWarp the
+    // operand tiles (onto the leader's full barrier), warp kSfProdWarp the
+    // scale atoms (onto this CTA's landing barrier).  Every copy instruction
+    // and barrier operation costs its issuing thread ~60-100 cycles, so one
+    // thread issuing all of a stage (~840 cycles per 256-deep K step,
+    // measured) rather than the MMAs set the pace of the main loop.
     if (lane == 0) {
+      const bool tile_role = warp == Cfg::kProdWarp;
       const uint64_t pol = policy_evict_normal();
       const CUtensorMap* tmap_b = rank == 0 ? &p.tmap_b1 : &p.tmap_b2;
       int stage = 0;
@@ -183,25 +199,28 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
           }
           const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
           const uint32_t sb = sa + Cfg::kABytes;
-          const uint32_t ssf = sb + Cfg::kBBytes;
-          // scales first, on this CTA's own landing barrier
-          const uint32_t landed = smem_u32(&bar_sf_landed[stage]);
-          mbar_arrive_expect_tx(landed, Cfg::kSfaBytes + 2 * Cfg::kSfbBytes);
-          const size_t so = (size_t)kb * kSfStageBytes;
-          // [SFA][SFB1 block 0 (, 1)][SFB2 block 0 (, 1)]
-          const uint32_t sb1 = ssf + Cfg::kSfaBytes, sb2 = sb1 + Cfg::kSfbBytes;
-          bulk_load(ssf, sfa_t + so, kSfStageBytes, landed, pol);
-          bulk_load(sb1, sfb1_0 + so, kSfStageBytes, landed, pol);
-          bulk_load(sb2, sfb2_0 + so, kSfStageBytes, landed, pol);
-          if constexpr (Cfg::kSfbBlocks == 2) {
-            bulk_load(sb1 + kSfStageBytes, sfb1_1 + so, kSfStageBytes, landed, pol);
-            bulk_load(sb2 + kSfStageBytes, sfb2_1 + so, kSfStageBytes, landed, pol);
+          if (tile_role) {
+            // operand tiles: both CTAs' bytes complete on the leader's stage barrier
+            const uint32_t full = mapa_shared(smem_u32(&bar_full[stage]), 0);
+            if (leader) mbar_arrive_expect_tx(smem_u32(&bar_full[stage]), Cfg::kPairTxBytes);
+            tma_load_3d_pair(sa, &p.tmap_a, full, kb * 128, m0, tc.l, pol);
+            tma_load_3d_pair(sb, tmap_b, full, kb * 128, n0, tc.l, pol);
+          } else {
+            // scales, on this CTA's own landing barrier:
+            // [SFA][SFB1 block 0 (, 1)][SFB2 block 0 (, 1)]
+            const uint32_t ssf = sb + Cfg::kBBytes;
+            const uint32_t landed = smem_u32(&bar_sf_landed[stage]);
+            mbar_arrive_expect_tx(landed, Cfg::kSfaBytes + 2 * Cfg::kSfbBytes);
+            const size_t so = (size_t)kb * kSfStageBytes;
+            const uint32_t sb1 = ssf + Cfg::kSfaBytes, sb2 = sb1 + Cfg::kSfbBytes;
+            bulk_load(ssf, sfa_t + so, kSfStageBytes, landed, pol);
+            bulk_load(sb1, sfb1_0 + so, kSfStageBytes, landed, pol);
+            bulk_load(sb2, sfb2_0 + so, kSfStageBytes, landed, pol);
+            if constexpr (Cfg::kSfbBlocks == 2) {
+              bulk_load(sb1 + kSfStageBytes, sfb1_1 + so, kSfStageBytes, landed, pol);
+              bulk_load(sb2 + kSfStageBytes, sfb2_1 + so, kSfStageBytes, landed, pol);
+            }
           }
-          // operand tiles: both CTAs' bytes complete on the leader's stage barrier
-          const uint32_t full = mapa_shared(smem_u32(&bar_full[stage]), 0);
-          if (leader) mbar_arrive_expect_tx(smem_u32(&bar_full[stage]), Cfg::kPairTxBytes);
-          tma_load_3d_pair(sa, &p.tmap_a, full, kb * 128, m0, tc.l, pol);
-          tma_load_3d_pair(sb, tmap_b, full, kb * 128, n0, tc.l, pol);
           issued |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == kStages) stage = 0, phase ^= 1u;
@@ -210,8 +229,8 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
       if (!ok) {  // in-flight copies land before the CTA winds down
         for (int s = 0; s < kStages; ++s)
           if ((issued >> s) & 1u) {
-            ctl.drain(smem_u32(&bar_sf_landed[s]), (last_phase >> s) & 1u);
-            if (leader) ctl.drain(smem_u32(&bar_full[s]), (last_phase >> s) & 1u);
+            if (!tile_role) ctl.drain(smem_u32(&bar_sf_landed[s]), (last_phase >> s) & 1u);
+            else if (leader) ctl.drain_copies(smem_u32(&bar_full[s]), (last_phase >> s) & 1u);
           }
       }
     }
@@ -234,8 +253,11 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
         tc_fence_after();
         const uint32_t d_acc = tmem + acc * Cfg::kAccCols;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          if (!ctl.wait(smem_u32(&bar_full[stage]), phase, kDevTimeoutTmaFull) ||
-              !ctl.wait(smem_u32(&bar_sf_full[stage]), phase, kDevTimeoutScales)) {
+          // both CTAs' operand tiles landed and scales staged: one barrier
+          // counts all of it, so this thread checks one barrier per K step
+          // (each check costs it ~100 cycles, and its loop sets the pace of
+          // small tiles)
+          if (!ctl.wait(smem_u32(&bar_full[stage]), phase, kDevTimeoutTmaFull)) {
             ok = false;
             break;
           }
@@ -261,7 +283,7 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
         ctl.drain(smem_u32(&bar_drain), 0);
       }
     }
-  } else if (warp >= Cfg::kEpiWarps + 2) {
+  } else if (warp >= Cfg::kSfWarp0) {
     // ------------------------------------------------------------ scale staging (both CTAs)
     // Warp w writes TMEM lanes [32*(w%4), +32) of its own CTA.  Lane i of every
     // quadrant receives row i of each atom column the MMA reads: SFA atom j in
@@ -326,7 +348,7 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&bar_sf_full[stage]), 0));
+        if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&bar_full[stage]), 0));
         if (++stage == kStages) stage = 0, phase ^= 1u;
       }
     }
@@ -390,7 +412,7 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
         for (int e = 8 * kC16; e < 32; ++e) w[e] = 0u;
       }
       acc_phase ^= 1u;
-      // kCW columns per row (48: three 32-byte chunks of a line, 64: a line)
+      // kCW columns per row (32 / 48: two / three 32-byte chunks of a line, 64: a line)
       const int row0 = tc.mp * 2 * kBM + (int)rank * kBM + quad * 32;
       const int col0 = tc.nb * Cfg::kBN + kCW * part;
       __half* c_line0 = p.c + ((size_t)tc.l * p.m + row0) * (size_t)p.n + col0;

@@ -203,7 +203,7 @@ grouped_gemm_kernel(const __grid_constant__ P p) {
   __shared__ typename Sched::Storage s_sched;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_full[kStages], bar_empty[kStages];
-  __shared__ uint64_t bar_sf_landed[kStages], bar_sf_full[kStages];
+  __shared__ uint64_t bar_sf_landed[kStages];
   __shared__ uint64_t bar_acc_full[kAccBufs], bar_acc_empty[kAccBufs];
   __shared__ uint64_t bar_drain;
   __shared__ uint32_t s_tmem_base;
@@ -216,10 +216,10 @@ grouped_gemm_kernel(const __grid_constant__ P p) {
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      mbar_init(smem_u32(&bar_full[s]), 1);
+      // the producer's expect_tx arrival + one per staging warp (+ the TMA bytes)
+      mbar_init(smem_u32(&bar_full[s]), 1 + Cfg::kSfWarps);
       mbar_init(smem_u32(&bar_empty[s]), 1);
       mbar_init(smem_u32(&bar_sf_landed[s]), 1);
-      mbar_init(smem_u32(&bar_sf_full[s]), Cfg::kSfWarps);
     }
     for (int b = 0; b < kAccBufs; ++b) {
       mbar_init(smem_u32(&bar_acc_full[b]), 1);
@@ -307,7 +307,7 @@ grouped_gemm_kernel(const __grid_constant__ P p) {
         for (int s = 0; s < kStages; ++s)
           if (issued[s]) {
             ctl.drain(smem_u32(&bar_sf_landed[s]), last_phase[s]);
-            ctl.drain(smem_u32(&bar_full[s]), last_phase[s]);
+            ctl.drain_copies(smem_u32(&bar_full[s]), last_phase[s]);
           }
       }
     }
@@ -330,9 +330,11 @@ grouped_gemm_kernel(const __grid_constant__ P p) {
         tc_fence_after();
         const uint32_t d = tmem + acc * kBN;
         for (int kb = 0; kb < k_blocks; ++kb) {
-          // operand tiles landed, and the stage's scales staged into TMEM
-          if (!ctl.wait(smem_u32(&bar_full[stage]), phase, kDevTimeoutTmaFull) ||
-              !ctl.wait(smem_u32(&bar_sf_full[stage]), phase, kDevTimeoutScales)) {
+          // operand tiles landed and the stage's scales staged into TMEM: one
+          // barrier counts both (the TMA bytes and one arrival per staging
+          // warp), so this thread checks one barrier per K step (each check
+          // costs it ~100 cycles, and its loop sets the pace of small tiles)
+          if (!ctl.wait(smem_u32(&bar_full[stage]), phase, kDevTimeoutTmaFull)) {
             ok = false;
             break;
           }
@@ -402,7 +404,7 @@ grouped_gemm_kernel(const __grid_constant__ P p) {
         tmem_st_wait();
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&bar_sf_full[stage]));
+        if (lane == 0) mbar_arrive(smem_u32(&bar_full[stage]));
         if (++stage == kStages) stage = 0, phase ^= 1u;
       }
     }

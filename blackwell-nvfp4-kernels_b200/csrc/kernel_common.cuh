@@ -64,6 +64,15 @@ struct AbortCtl {
     while (!mbar_try_wait(bar, parity))
       if (clock64() - t0 > limit) return;
   }
+  // The same for a stage barrier that also counts other warps' arrivals:
+  // after an abort those may never come, so the phase may never complete;
+  // the copies themselves land within microseconds, so give them ~30 us.
+  __device__ __forceinline__ void drain_copies(uint32_t bar, uint32_t parity) const {
+    const long long t0 = clock64();
+    const long long cap = limit < (1LL << 16) ? limit : (1LL << 16);
+    while (!mbar_try_wait(bar, parity))
+      if (clock64() - t0 > cap) return;
+  }
 };
 
 // silu(g) * u in fp32: g / (1 + e^-g) * u, using the fast exp and divide
