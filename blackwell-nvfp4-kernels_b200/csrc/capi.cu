@@ -663,26 +663,38 @@ int run_dual(DeviceState* d, const void* a, const void* b1, const void* b2, cons
   // when the tiles leave SMs idle; 64-wide tiles on request), or the CTA-pair
   // kernel (NVFP4_DUAL_KERNEL=pair; 96-wide tiles with NVFP4_DUAL_BN=96),
   // which loads a third fewer operand bytes per SM but measures ~3% slower
-  // on configuration 1 (440 vs 428 us).  Automatic choice of the pair: one
-  // pair block per batch (128 < M <= 256: both SMs of a pair hold real rows
-  // and B is fetched once instead of once per 128-row block), the
-  // single-CTA kernel would split K, at least 48 CTAs, at most 32 K blocks
-  // (longer K favours the split).  Measured (us, single vs pair):
-  // 256x3072x4096 24.5 / 21.9, 256x4096x7168 30.3 / 28.4, 200x4096x7168
-  // 30.2 / 29.0, 256x7168x2048 19.7 / 19.9; kept single: 256x2048x7168
-  // 26.4 / 27.4, 256x1024x16384 28.3 / 42.1.
+  // on configuration 1 (440 vs 428 us).  Automatic choice of the pair, for
+  // 12 to 32 K blocks (fewer favour the single kernel's shorter pipeline
+  // fill, more its K split), from the reference's benchmark shapes timed as
+  // its harness times them (us, pair vs single-CTA kernel):
+  //   one 256-row pair block (128 < M <= 256) where the single kernel would
+  //   leave SMs idle: 64-wide pair tiles when they make 64..num_sms CTAs
+  //   (256x4096x7168 17.2 / 18.8, 256x3072x4096 12.3 / 12.6, 256x2048x7168
+  //   16.2 / 17.1), else 128-wide when those make 48..num_sms CTAs;
+  //   two pair blocks (256 < M <= 512), when the 128-wide pair tiles fit one
+  //   wave (512x4096x7168 18.7 / 19.3, 512x3072x7168 18.5 / 19.0,
+  //   384x4096x7168 18.6 / 19.2);
+  //   otherwise single (256x7168x2048, 8 K blocks: 10.8 / 10.4;
+  //   256x512x1024: 7.0 / 6.9).
   bool pair = kn.dual_kernel == 1;
+  int pair_bn = kn.dual_bn;
   if (kn.dual_kernel == 0 && kn.dual_bn == 0 && kn.dual_splits == 0 && kn.dual_cluster == 0 &&
-      m > 128 && m <= 256) {
+      p.k_blocks >= 12 && p.k_blocks <= 32) {
     const int single_tiles = l * ((m + kBM - 1) / kBM) * ((n + 127) / 128);
-    const int pair_ctas = 2 * l * ((n + 127) / 128);
-    pair = single_tiles < d->num_sms && pair_ctas >= 48 && pair_ctas <= d->num_sms && p.k_blocks <= 32;
+    const int ctas128 = 2 * l * ((m + 2 * kBM - 1) / (2 * kBM)) * ((n + 127) / 128);
+    const int ctas64 = 2 * l * ((m + 2 * kBM - 1) / (2 * kBM)) * ((n + 63) / 64);
+    if (m > 128 && m <= 256 && single_tiles < d->num_sms) {
+      if (ctas64 >= 64 && ctas64 <= d->num_sms) pair = true, pair_bn = 64;
+      else if (ctas128 >= 48 && ctas128 <= d->num_sms) pair = true, pair_bn = 128;
+    } else if (m > 256 && m <= 512 && ctas128 >= 48 && ctas128 <= d->num_sms) {
+      pair = true, pair_bn = 128;
+    }
   }
   if (pair) {
-    if (kn.dual_bn == 96)
+    if (pair_bn == 96)
       return launch_dual_2sm<96, 5>(d, 3, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
                                     kn.dual_group_m, al, stream);
-    if (kn.dual_bn == 64)
+    if (pair_bn == 64)
       return launch_dual_2sm<64, 7>(d, 15, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
                                     kn.dual_group_m, al, stream);
     return launch_dual_2sm<128, 5>(d, 14, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
