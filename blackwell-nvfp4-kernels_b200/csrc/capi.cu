@@ -105,7 +105,8 @@ struct Knobs {
   int dual_group_m = 32;   // NVFP4_DUAL_GROUP_M (measured: 16 -> 32 saves ~1.5% on 8192x14336x4096)
   int dual_splits = 0;     // NVFP4_DUAL_SPLITS (0 = automatic)
   int dual_bn = 0;         // NVFP4_DUAL_BN (64 / 128, or 64 / 96 / 128 for the pair kernel; 0 = automatic)
-  int dual_kernel = 0;     // NVFP4_DUAL_KERNEL: 0 automatic, 1 pair (CTA-pair kernel), 2 single
+  int dual_kernel = 0;     // NVFP4_DUAL_KERNEL: 0 automatic, 1 pair (CTA-pair kernel), 2 single,
+                           // 3 paircp (CTA-pair kernel, scale-copy mode)
   int dual_cluster = 0;    // NVFP4_DUAL_CLUSTER: 0 automatic, 1 off, 2 / 4 forced cluster split-K
   int grouped_bn = 0;      // NVFP4_GROUPED_BN (128 / 256; 0 = automatic)
   bool pdl = true;         // NVFP4_PDL=0: launch the GEMMs without programmatic dependent launch
@@ -126,7 +127,10 @@ Knobs read_knobs() {
     else if ((x = val("DUAL_SPLITS"))) k.dual_splits = atoi(x);
     else if ((x = val("DUAL_BN"))) k.dual_bn = atoi(x);
     else if ((x = val("DUAL_KERNEL")))
-      k.dual_kernel = strcmp(x, "pair") == 0 ? 1 : strcmp(x, "single") == 0 ? 2 : 0;
+      k.dual_kernel = strcmp(x, "pair") == 0     ? 1
+                      : strcmp(x, "single") == 0 ? 2
+                      : strcmp(x, "paircp") == 0 ? 3
+                                                 : 0;
     else if ((x = val("DUAL_CLUSTER"))) k.dual_cluster = atoi(x);
     else if ((x = val("GROUPED_BN"))) k.grouped_bn = atoi(x);
     else if ((x = val("PDL"))) k.pdl = atoi(x) != 0;
@@ -236,6 +240,29 @@ int encode_operand(CUtensorMap* map, const void* base, int rows, int k, int l, i
   const MapKey key{reinterpret_cast<uintptr_t>(base), rows, k, l, box_rows};
   return cached_map(map, key,
                     [&] { return encode_operand_uncached(map, base, rows, k, l, box_rows); });
+}
+
+// 2-D view [atoms][128 x 32-bit] of a permuted scale tensor (512-byte atoms),
+// box {128, 4}: the four atoms of one 256-deep K step of one 128-row block.
+int encode_sf_atoms_uncached(CUtensorMap* map, const void* base, int atoms) {
+  const cuuint64_t dims[2] = {128u, (cuuint64_t)atoms};
+  const cuuint64_t strides[1] = {(cuuint64_t)kSfAtom};
+  const cuuint32_t box[2] = {128u, (cuuint32_t)(kBK / kKStep)};
+  const cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT32, 2, const_cast<void*>(base), dims,
+                        strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(NVFP4_ERR_CUDA, "cuTensorMapEncodeTiled failed (%d) for %d scale atoms", (int)r,
+                atoms);
+  return NVFP4_OK;
+}
+
+int encode_sf_atoms(CUtensorMap* map, const void* base, int atoms) {
+  // k = -1 keeps these keys apart from the operand maps'
+  const MapKey key{reinterpret_cast<uintptr_t>(base), atoms, -1, 0, kBK / kKStep};
+  return cached_map(map, key, [&] { return encode_sf_atoms_uncached(map, base, atoms); });
 }
 
 int check_launch(const char* what) {
@@ -502,13 +529,14 @@ int launch_dual(DeviceState* d, int slot, DualParams& p, int forced_splits, int 
                      "dual_gemm_kernel");
 }
 
-// CTA-pair kernel: kBN-column tiles (128 or 96), M=256 x N=2*kBN MMAs, one accumulator.
-template <int kBN, int kStages>
+// CTA-pair kernel: kBN-column tiles (128, 96 or 64), M=256 MMAs, one
+// accumulator; scales staged by warps, or (kCp) copied by the MMA thread.
+template <int kBN, int kStages, bool kCp = false>
 int launch_dual_2sm(DeviceState* d, int slot, const void* a, const void* b1, const void* b2,
                     const void* sfa, const void* sfb1, const void* sfb2, void* c, int m, int n,
                     int k, int l, int group_m, const DualAlloc& al, cudaStream_t stream) {
-  using Cfg = Dual2smCfg<kBN, kStages>;
-  auto kern = dual_gemm_2sm_kernel<kBN, kStages>;
+  using Cfg = Dual2smCfg<kBN, kStages, kCp>;
+  auto kern = dual_gemm_2sm_kernel<kBN, kStages, kCp>;
   int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
   if (rc) return rc;
   Dual2smParams p;
@@ -528,9 +556,20 @@ int launch_dual_2sm(DeviceState* d, int slot, const void* a, const void* b1, con
   p.c_lines32 = (n % 16 == 0) && (reinterpret_cast<uintptr_t>(c) % 32 == 0);
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
+  const int b_box = kCp ? kBN / 2 : kBN;   // scale-copy mode: each CTA loads half of B1 and of B2
   if ((rc = encode_dual_operand(al, &p.tmap_a, a, m, k, l, kBM))) return rc;
-  if ((rc = encode_dual_operand(al, &p.tmap_b1, b1, n, k, l, Cfg::kBN))) return rc;
-  if ((rc = encode_dual_operand(al, &p.tmap_b2, b2, n, k, l, Cfg::kBN))) return rc;
+  if ((rc = encode_dual_operand(al, &p.tmap_b1, b1, n, k, l, b_box))) return rc;
+  if ((rc = encode_dual_operand(al, &p.tmap_b2, b2, n, k, l, b_box))) return rc;
+  if (kCp) {
+    const int rest_k = k / kKStep;
+    const int a_atoms = l * p.sfa_blocks * rest_k, b_atoms = l * p.sfb_blocks * rest_k;
+    auto enc = [&](CUtensorMap* map, const void* base, int atoms) {
+      return al.fixed ? encode_sf_atoms_uncached(map, base, atoms) : encode_sf_atoms(map, base, atoms);
+    };
+    if ((rc = enc(&p.tmap_sfa, sfa, a_atoms))) return rc;
+    if ((rc = enc(&p.tmap_sfb1, sfb1, b_atoms))) return rc;
+    if ((rc = enc(&p.tmap_sfb2, sfb2, b_atoms))) return rc;
+  }
   const int pairs = p.tiles < d->num_sms / 2 ? p.tiles : d->num_sms / 2;
   return launch_gemm(kern, (unsigned)(2 * pairs), Cfg::kThreads, Cfg::kSmemBytes, stream, p, 0,
                      "dual_gemm_2sm_kernel");
@@ -689,6 +728,13 @@ int run_dual(DeviceState* d, const void* a, const void* b1, const void* b2, cons
     } else if (m > 256 && m <= 512 && ctas128 >= 48 && ctas128 <= d->num_sms) {
       pair = true, pair_bn = 128;
     }
+  }
+  if (kn.dual_kernel == 3) {
+    if (pair_bn == 128)
+      return launch_dual_2sm<128, 5, true>(d, 17, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
+                                           kn.dual_group_m, al, stream);
+    return launch_dual_2sm<64, 7, true>(d, 16, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
+                                        kn.dual_group_m, al, stream);
   }
   if (pair) {
     if (pair_bn == 96)

@@ -196,7 +196,7 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
 
   if (warp == kEpiWarps) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    if (elect_one()) {   // one thread; uniform registers for the issue
       const uint64_t pol = policy_evict_normal();
       const int rest_k = p.k_blocks * (kBK / kKStep);  // 64-K atoms per 128 rows
       const size_t sfa_l = (size_t)p.m_blocks * rest_k * kSfAtom;
@@ -252,10 +252,11 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
     }
   } else if (warp == kEpiWarps + 1) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (elect_one()) {   // one thread; uniform registers for the issue
       // 128-wide tiles: one M=128, N=256 MMA per 64-K step over [B1 tile ; B2 tile];
       // 64-wide tiles: two N=64 MMAs (gate, up)
       constexpr uint32_t idesc = idesc_mxf4nvf4<kBM, kBN == 128 ? 2 * kBN : kBN>();
+      const uint64_t a_desc0 = kmajor_sw128_desc(smem_base);   // stage 0's A tile
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -283,26 +284,24 @@ dual_gemm_kernel(const __grid_constant__ DualParams p) {
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
-          const uint32_t sb = sa + Cfg::kABytes;             // B1 rows then B2 rows
+          const uint64_t da0 = desc_advance(a_desc0, (uint32_t)stage * Cfg::kStageBytes);
+          const uint64_t db0 = desc_advance(da0, Cfg::kABytes);   // B1 rows then B2 rows
           // scales of k-step j: SFA in [sf_a+4j, +4), SFB1 | SFB2 in [sf_b+8j, +8)
           const uint32_t sf_a = tmem + Cfg::kSfCol + stage * Cfg::kSfBufCols;
           const uint32_t sf_b = sf_a + 16;
           #pragma unroll
           for (int j = 0; j < kBK / kKStep; ++j) {
-            const uint64_t da = kmajor_sw128_desc(sa + 32 * j);
+            const uint64_t da = desc_advance(da0, 32 * j), db = desc_advance(db0, 32 * j);
             const uint32_t accum = kSplitK ? ((kb != kr.kb0) || (j != 0)) : ((kb | j) != 0);
             if constexpr (kBN == 128) {
               // one N=256 MMA over [B1 ; B2]: the 8 scale columns are exactly
               // SFB1 rows 0..127 then SFB2 rows 0..127
-              tc_mma_nvf4(d_acc, da, kmajor_sw128_desc(sb + 32 * j), idesc, sf_a + 4 * j,
-                          sf_b + 8 * j, accum);
+              tc_mma_nvf4(d_acc, da, db, idesc, sf_a + 4 * j, sf_b + 8 * j, accum);
             } else {
               // 64-row halves of the atoms sit in columns {0,1} or {2,3}: two N=64 MMAs
-              tc_mma_nvf4(d_acc, da, kmajor_sw128_desc(sb + 32 * j), idesc, sf_a + 4 * j,
-                          sf_b + 8 * j + sub, accum);
-              tc_mma_nvf4(d_acc + kBN, da, kmajor_sw128_desc(sb + Cfg::kBBytes + 32 * j), idesc,
-                          sf_a + 4 * j, sf_b + 8 * j + 4 + sub, accum);
+              tc_mma_nvf4(d_acc, da, db, idesc, sf_a + 4 * j, sf_b + 8 * j + sub, accum);
+              tc_mma_nvf4(d_acc + kBN, da, desc_advance(db, Cfg::kBBytes), idesc, sf_a + 4 * j,
+                          sf_b + 8 * j + 4 + sub, accum);
             }
           }
           tc_commit(smem_u32(&bar_empty[stage]));  // frees the stage (and its scale buffer)

@@ -46,6 +46,9 @@ struct Dual2smParams {
   CUtensorMap tmap_a;    // bytes [L][M][K/2], box {128 B, 128 rows, 1}
   CUtensorMap tmap_b1;   // bytes [L][N][K/2], box {128 B, kBN rows, 1}
   CUtensorMap tmap_b2;
+  // scale-copy mode only: the scale atoms as 2-D [atoms][128 x 32-bit] maps,
+  // box {128, 4} (one 256-deep K step of one 128-row block)
+  CUtensorMap tmap_sfa, tmap_sfb1, tmap_sfb2;
   const uint8_t* sfa;    // permuted scale atoms [L][ceil(M/128)][K/64][512]
   const uint8_t* sfb1;   // [L][ceil(N/128)][K/64][512]
   const uint8_t* sfb2;
@@ -59,10 +62,16 @@ struct Dual2smParams {
   long long wait_limit;
 };
 
-template <int kBN_, int kStages>
+template <int kBN_, int kStages, bool kCp_ = false>
 struct Dual2smCfg {
   static constexpr int kBN = kBN_;                     // C columns per tile: 64, 96 or 128
-  static constexpr int kNmma = 2 * kBN;                // pair MMA N = [B1 tile ; B2 tile]
+  // scale-copy mode: each CTA loads half of the tile's B1 rows and half of
+  // its B2 rows, the scale atoms arrive by TMA on the stage barrier, and the
+  // MMA thread copies them into TMEM itself (tcgen05.cp) before two MMAs
+  // (gate, up) of N = kBN per K step; no staging warps
+  static constexpr bool kCp = kCp_;
+  static constexpr int kNmma = kCp ? kBN : 2 * kBN;    // pair MMA N: [B1 tile ; B2 tile], or one of them
+  static constexpr int kBHalfBytes = (kBN / 2) * kBK / 2;   // scale-copy mode: B1 or B2 rows of one CTA
   static constexpr int kGroups = kBN / 32;             // 32-row groups per B tile
   static constexpr int kSfbBlocks = kBN == 96 ? 2 : 1;    // 128-row atom blocks covering a tile
   static constexpr int kABytes = kBM * kBK / 2;        // 16 KB
@@ -70,10 +79,12 @@ struct Dual2smCfg {
   static constexpr int kSfaBytes = kSfStageBytes;      // 4 atoms of this CTA's A rows
   static constexpr int kSfbBytes = kSfbBlocks * kSfStageBytes;   // per B operand
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + 2 * kSfbBytes;   // 30-38 KB
-  static constexpr int kPairTxBytes = 2 * (kABytes + kBBytes);
+  // bytes both CTAs' copies of a stage count on the leader's stage barrier
+  static constexpr int kPairTxBytes = kCp ? 2 * (kABytes + kBBytes + kSfaBytes + 2 * kSfbBytes)
+                                          : 2 * (kABytes + kBBytes);
   static constexpr int kEpiWarps = 8;                   // 2 per TMEM quadrant
   static constexpr int kColsPerWarp = kBN / 2;         // 32, 48 or 64 columns of gate and of up
-  static constexpr int kSfWarps = 4;
+  static constexpr int kSfWarps = kCp ? 0 : 4;
   // warp roles: epilogue [0, 8), tile producer 8, MMA 9, scale producer 10,
   // scale staging [11, 15)
   static constexpr int kProdWarp = kEpiWarps, kMmaWarp = kEpiWarps + 1;
@@ -82,12 +93,13 @@ struct Dual2smCfg {
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024;
   static constexpr int kTmemCols = 512;
   static constexpr int kAccBufs = 1;
-  static constexpr int kAccCols = kNmma;
+  static constexpr int kAccCols = 2 * kBN;             // gate columns, then up columns
   static constexpr int kSfCol = kAccBufs * kAccCols;   // 2 * kBN
   static constexpr int kSfBufCols = 48;                // per stage: SFA 4x4 + SFB 4x8 (6 used)
   static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned");
   static_assert(kSfCol + kStages * kSfBufCols <= kTmemCols, "TMEM budget: one scale buffer per stage");
   static_assert(kBN == 64 || kBN == 96 || kBN == 128, "tile width");
+  static_assert(!kCp || kBN != 96, "scale-copy mode: a tile lies in one 128-row scale block");
 };
 
 struct PairTile2 { int l, mp, nb; };
@@ -107,10 +119,10 @@ __device__ __forceinline__ PairTile2 pair2_tile_coord(const Dual2smParams& p, in
   return tc;
 }
 
-template <int kBN, int kStages>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Dual2smCfg<kBN, kStages>::kThreads, 1)
+template <int kBN, int kStages, bool kCp>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Dual2smCfg<kBN, kStages, kCp>::kThreads, 1)
 dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
-  using Cfg = Dual2smCfg<kBN, kStages>;
+  using Cfg = Dual2smCfg<kBN, kStages, kCp>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_full[kStages], bar_empty[kStages];
   __shared__ uint64_t bar_sf_landed[kStages];
@@ -130,7 +142,7 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
     for (int s = 0; s < kStages; ++s) {
       // the leader's expect_tx arrival + one per staging warp of both CTAs (+ the
       // TMA bytes of both CTAs)
-      mbar_init(smem_u32(&bar_full[s]), 1 + 2 * Cfg::kSfWarps);
+      mbar_init(smem_u32(&bar_full[s]), 1 + 2 * Cfg::kSfWarps);   // (scale-copy mode: 1)
       mbar_init(smem_u32(&bar_empty[s]), 1);
       mbar_init(smem_u32(&bar_sf_landed[s]), 1);
     }
@@ -145,7 +157,15 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
   }
   if (warp == Cfg::kProdWarp && lane == 0) {
     tma_prefetch_desc(&p.tmap_a);
-    tma_prefetch_desc(rank == 0 ? &p.tmap_b1 : &p.tmap_b2);
+    if constexpr (kCp) {
+      tma_prefetch_desc(&p.tmap_b1);
+      tma_prefetch_desc(&p.tmap_b2);
+      tma_prefetch_desc(&p.tmap_sfa);
+      tma_prefetch_desc(&p.tmap_sfb1);
+      tma_prefetch_desc(&p.tmap_sfb2);
+    } else {
+      tma_prefetch_desc(rank == 0 ? &p.tmap_b1 : &p.tmap_b2);
+    }
   }
   if (warp == Cfg::kMmaWarp) tmem_alloc_pair<Cfg::kTmemCols>(smem_u32(&s_tmem_base));
   tc_fence_before();
@@ -167,7 +187,10 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
     // and barrier operation costs its issuing thread ~60-100 cycles, so one
     // thread issuing all of a stage (~840 cycles per 256-deep K step,
     // measured) rather than the MMAs set the pace of the main loop.
-    if (lane == 0) {
+    // elect.sync rather than lane == 0: the compiler then knows one thread
+    // runs the region and keeps its addresses and descriptors in uniform
+    // registers, which the copy and MMA instructions take directly
+    if (elect_one()) {
       const bool tile_role = warp == Cfg::kProdWarp;
       const uint64_t pol = policy_evict_normal();
       const CUtensorMap* tmap_b = rank == 0 ? &p.tmap_b1 : &p.tmap_b2;
@@ -204,7 +227,25 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
             const uint32_t full = mapa_shared(smem_u32(&bar_full[stage]), 0);
             if (leader) mbar_arrive_expect_tx(smem_u32(&bar_full[stage]), Cfg::kPairTxBytes);
             tma_load_3d_pair(sa, &p.tmap_a, full, kb * 128, m0, tc.l, pol);
-            tma_load_3d_pair(sb, tmap_b, full, kb * 128, n0, tc.l, pol);
+            if constexpr (kCp) {
+              // this CTA's half of the tile's B1 rows, then of its B2 rows
+              const int nb0 = n0 + (int)rank * (kBN / 2);
+              tma_load_3d_pair(sb, &p.tmap_b1, full, kb * 128, nb0, tc.l, pol);
+              tma_load_3d_pair(sb + Cfg::kBHalfBytes, &p.tmap_b2, full, kb * 128, nb0, tc.l, pol);
+            } else {
+              tma_load_3d_pair(sb, tmap_b, full, kb * 128, n0, tc.l, pol);
+            }
+          } else if constexpr (kCp) {
+            // scale atoms [SFA][SFB1][SFB2] (4 atoms each), also counted on the
+            // leader's stage barrier: the MMA thread copies them to TMEM itself
+            const uint32_t ssf = sb + Cfg::kBBytes;
+            const uint32_t full = mapa_shared(smem_u32(&bar_full[stage]), 0);
+            const int ka = kb * (kBK / kKStep);
+            const int a_atom = (tc.l * p.sfa_blocks + ablk) * rest_k + ka;
+            const int b_atom = (tc.l * p.sfb_blocks + blk0) * rest_k + ka;
+            tma_load_2d_pair(ssf, &p.tmap_sfa, full, 0, a_atom, pol);
+            tma_load_2d_pair(ssf + Cfg::kSfaBytes, &p.tmap_sfb1, full, 0, b_atom, pol);
+            tma_load_2d_pair(ssf + Cfg::kSfaBytes + Cfg::kSfbBytes, &p.tmap_sfb2, full, 0, b_atom, pol);
           } else {
             // scales, on this CTA's own landing barrier:
             // [SFA][SFB1 block 0 (, 1)][SFB2 block 0 (, 1)]
@@ -227,19 +268,24 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
         }
       }
       if (!ok) {  // in-flight copies land before the CTA winds down
+        // (a peer's copies land on the leader's stage barriers: the leader
+        // drains them, and the closing cluster barrier holds the peer)
         for (int s = 0; s < kStages; ++s)
           if ((issued >> s) & 1u) {
-            if (!tile_role) ctl.drain(smem_u32(&bar_sf_landed[s]), (last_phase >> s) & 1u);
+            if (!tile_role && !kCp) ctl.drain(smem_u32(&bar_sf_landed[s]), (last_phase >> s) & 1u);
             else if (leader) ctl.drain_copies(smem_u32(&bar_full[s]), (last_phase >> s) & 1u);
           }
       }
     }
   } else if (warp == Cfg::kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer (leader only)
-    if (leader && lane == 0) {
+    if (leader && elect_one()) {
       constexpr uint32_t idesc = (1u << 7) | (1u << 10) | ((uint32_t)(Cfg::kNmma >> 3) << 17) |
                                  ((uint32_t)(256 >> 4) << 24);   // M=256, N=2*kBN, e2m1 x e2m1, e4m3 scales
       constexpr uint16_t kBoth = 0x3;
+      const uint64_t a_desc0 = kmajor_sw128_desc(smem_base);   // stage 0's A tile
+      // stage 0's first SFA atom (scale-copy mode)
+      const uint64_t sf_desc0 = sf_atom_desc(smem_base + Cfg::kABytes + Cfg::kBBytes);
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -252,6 +298,9 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
         }
         tc_fence_after();
         const uint32_t d_acc = tmem + acc * Cfg::kAccCols;
+        // scale-copy mode: the tile's B rows start at column (n0 % 128) / 32
+        // of their 128-row scale atoms
+        const uint32_t b_col = kCp ? (uint32_t)((pair2_tile_coord(p, t).nb * kBN) % 128) / 32u : 0u;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           // both CTAs' operand tiles landed and scales staged: one barrier
           // counts all of it, so this thread checks one barrier per K step
@@ -262,14 +311,38 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
-          const uint32_t sb = sa + Cfg::kABytes;
+          // descriptors of this stage's tiles and atoms: the stage-0 ones advanced
+          const uint32_t so = (uint32_t)stage * Cfg::kStageBytes;
+          const uint64_t da = desc_advance(a_desc0, so);
+          const uint64_t db = desc_advance(da, Cfg::kABytes);   // this CTA's B rows
           const uint32_t sf_a = tmem + Cfg::kSfCol + stage * Cfg::kSfBufCols;
           const uint32_t sf_b = sf_a + 16;
-          #pragma unroll
-          for (int j = 0; j < kBK / kKStep; ++j)
-            tc_mma_nvf4_pair(d_acc, kmajor_sw128_desc(sa + 32 * j), kmajor_sw128_desc(sb + 32 * j),
-                             idesc, sf_a + 4 * j, sf_b + 8 * j, (kb | j) != 0);
+          if constexpr (kCp) {
+            // per 64-deep step: the step's SFA, SFB1 and SFB2 atoms into TMEM
+            // (columns sf_a + 4j, sf_b + 4j, sf_b + 16 + 4j), then gate and up
+            // (A kept in the collector between them); the tensor pipe runs
+            // this thread's copies and MMAs in issue order
+            const uint64_t dsf = desc_advance(sf_desc0, so);
+            #pragma unroll
+            for (int j = 0; j < kBK / kKStep; ++j) {
+              const uint64_t dsa = desc_advance(dsf, j * kSfAtom);
+              tc_cp_pair_32x128b_x4(sf_a + 4 * j, dsa);
+              tc_cp_pair_32x128b_x4(sf_b + 4 * j, desc_advance(dsa, Cfg::kSfaBytes));
+              tc_cp_pair_32x128b_x4(sf_b + 16 + 4 * j, desc_advance(dsa, Cfg::kSfaBytes + Cfg::kSfbBytes));
+              const uint64_t daj = desc_advance(da, 32 * j), db1 = desc_advance(db, 32 * j);
+              const uint32_t acc_in = (kb | j) != 0;
+              tc_mma_nvf4_pair_ca<CollectorA::kFill>(d_acc, daj, db1, idesc, sf_a + 4 * j,
+                                                    sf_b + 4 * j + b_col, acc_in);
+              tc_mma_nvf4_pair_ca<CollectorA::kLastUse>(d_acc + kBN, daj,
+                                                       desc_advance(db1, Cfg::kBHalfBytes), idesc,
+                                                       sf_a + 4 * j, sf_b + 16 + 4 * j + b_col, acc_in);
+            }
+          } else {
+            #pragma unroll
+            for (int j = 0; j < kBK / kKStep; ++j)
+              tc_mma_nvf4_pair(d_acc, desc_advance(da, 32 * j), desc_advance(db, 32 * j), idesc,
+                               sf_a + 4 * j, sf_b + 8 * j, (kb | j) != 0);
+          }
           tc_commit_pair(smem_u32(&bar_empty[stage]), kBoth);   // stage (and scale buffer) free
           any = true;
           if (++stage == kStages) stage = 0, phase ^= 1u;
@@ -283,7 +356,7 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
         ctl.drain(smem_u32(&bar_drain), 0);
       }
     }
-  } else if (warp >= Cfg::kSfWarp0) {
+  } else if (!kCp && warp >= Cfg::kSfWarp0) {
     // ------------------------------------------------------------ scale staging (both CTAs)
     // Warp w writes TMEM lanes [32*(w%4), +32) of its own CTA.  Lane i of every
     // quadrant receives row i of each atom column the MMA reads: SFA atom j in

@@ -248,7 +248,7 @@ grouped_gemm_kernel(const __grid_constant__ P p) {
 
   if (warp == kProd) {
     // ------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    if (elect_one()) {   // one thread; uniform registers for the issue
       const uint64_t pol = policy_evict_normal();
       int stage = 0;
       uint32_t phase = 0;
@@ -313,8 +313,9 @@ grouped_gemm_kernel(const __grid_constant__ P p) {
     }
   } else if (warp == kMma) {
     // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    if (elect_one()) {   // one thread; uniform registers for the issue
       constexpr uint32_t idesc = idesc_mxf4nvf4<kBM, kBN>();
+      const uint64_t a_desc0 = kmajor_sw128_desc(smem_base);   // stage 0's A tile
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -339,14 +340,14 @@ grouped_gemm_kernel(const __grid_constant__ P p) {
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
-          const uint32_t sb = sa + Cfg::kABytes;
+          const uint64_t da = desc_advance(a_desc0, (uint32_t)stage * Cfg::kStageBytes);
+          const uint64_t db = desc_advance(da, Cfg::kABytes);
           // scales of k-step j: SFA in [sf_a+4j, +4), SFB atom a in [sf_b+4(atoms*j+a), +4)
           const uint32_t sf_a = tmem + Cfg::kSfCol + stage * Cfg::kSfBufCols;
           const uint32_t sf_b = sf_a + 16;
           #pragma unroll
           for (int j = 0; j < kBK / kKStep; ++j) {
-            tc_mma_nvf4(d, kmajor_sw128_desc(sa + 32 * j), kmajor_sw128_desc(sb + 32 * j), idesc,
+            tc_mma_nvf4(d, desc_advance(da, 32 * j), desc_advance(db, 32 * j), idesc,
                         sf_a + 4 * j, sf_b + 4 * Cfg::kSfbAtoms * j, (kb | j) != 0);
           }
           tc_commit(smem_u32(&bar_empty[stage]));   // frees the stage and its scale buffer

@@ -187,6 +187,14 @@ __device__ __forceinline__ uint64_t kmajor_sw128_desc(uint32_t saddr) {
   return smem_desc(saddr, 16, 1024, kLayoutSwizzle128B);
 }
 
+// The same descriptor `bytes` further on (bytes a multiple of 16).  Shared
+// memory addresses stay below 256 KB, so the 14-bit address field never
+// carries: the result equals the descriptor built from the new address, for
+// one 64-bit add instead of a mask, a shift and the ors.
+__device__ __forceinline__ uint64_t desc_advance(uint64_t desc, uint32_t bytes) {
+  return desc + (uint64_t)(bytes >> 4);
+}
+
 // Instruction descriptor, kind::mxf4nvf4: A and B e2m1 (format 1) K-major,
 // e4m3 scales (scale format 0), fp32 accumulate, N>>3 at [17,23), M>>4 at [24,29).
 template <int M, int N>
@@ -382,6 +390,32 @@ __device__ __forceinline__ void tma_load_3d_pair(uint32_t dst, const void* tmap,
       : "memory");
 }
 
+// 2-D tiled TMA load into this CTA's shared memory, bytes counted on an
+// mbarrier of either CTA of the pair (no multicast).
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const void* tmap, uint32_t bar_cluster,
+                                                 int c0, int c1, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(dst),
+      "l"(tmap), "r"(bar_cluster), "r"(c0), "r"(c1), "l"(policy)
+      : "memory");
+}
+
+// Descriptor of one 512-byte scale atom in shared memory as a 32-row x
+// 128-bit matrix without swizzle: 8-row core groups of 128 contiguous bytes.
+__device__ __forceinline__ uint64_t sf_atom_desc(uint32_t saddr) {
+  return smem_desc(saddr, 0, 128, kLayoutNone);
+}
+
+// Pair copy (issued by the leader): in each CTA of the pair, the 32 x 128-bit
+// matrix at the descriptor's address in that CTA's shared memory goes to TMEM
+// lanes [32q, 32q + 32) of every lane quadrant q, columns [taddr, taddr + 4):
+// row i of a scale atom lands in lane i of each quadrant.
+__device__ __forceinline__ void tc_cp_pair_32x128b_x4(uint32_t taddr, uint64_t s_desc) {
+  asm volatile("tcgen05.cp.cta_group::2.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(s_desc)
+               : "memory");
+}
+
 template <int kCols>
 __device__ __forceinline__ void tmem_alloc_pair(uint32_t dst_smem) {  // one warp in each CTA
   asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
@@ -408,6 +442,37 @@ __device__ __forceinline__ void tc_mma_nvf4_pair(uint32_t d_tmem, uint64_t a_des
       "}" ::"r"(d_tmem),
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
       : "memory");
+}
+
+// Pair MMA whose A operand stays in the tensor core's collector buffer for
+// the next MMA (kFill), or is taken from it and then released (kLastUse):
+// two MMAs over one A tile read A from shared memory once.
+enum class CollectorA { kNone, kFill, kLastUse };
+template <CollectorA kC>
+__device__ __forceinline__ void tc_mma_nvf4_pair_ca(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                                    uint32_t idesc, uint32_t sfa_tmem,
+                                                    uint32_t sfb_tmem, uint32_t accumulate) {
+  if constexpr (kC == CollectorA::kFill) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16.collector::a::fill"
+        " [%0], %1, %2, %3, [%4], [%5], p;\n\t"
+        "}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
+        : "memory");
+  } else if constexpr (kC == CollectorA::kLastUse) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %6, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::mxf4nvf4.block_scale.block16.collector::a::lastuse"
+        " [%0], %1, %2, %3, [%4], [%5], p;\n\t"
+        "}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(sfa_tmem), "r"(sfb_tmem), "r"(accumulate)
+        : "memory");
+  } else {
+    tc_mma_nvf4_pair(d_tmem, a_desc, b_desc, idesc, sfa_tmem, sfb_tmem, accumulate);
+  }
 }
 
 // Arrive once on the mbarrier at the same offset in every CTA of `cta_mask`

@@ -98,6 +98,22 @@ def test_dual_pair_kernel_edges(m, n, k, l, bn, monkeypatch):
     assert_close(run_dual(data), oracle_dual(data), f"dual {kernel} {m}x{n}x{k}x{l}")
 
 
+@pytest.mark.parametrize("bn", ["64", "128"])
+@pytest.mark.parametrize("m,n,k,l", DUAL_TASK_TESTS + DUAL_TASK_BENCH + [
+    (256, 128, 256, 1), (384, 640, 1024, 2), (200, 264, 512, 1), (130, 72, 768, 1), (1, 8, 256, 1),
+    (1000, 1000, 2048, 1), (100, 256, 1024, 3), (256, 4160, 2048, 1)])
+def test_dual_pair_scale_copy_mode(m, n, k, l, bn, monkeypatch):
+    """CTA-pair kernel in scale-copy mode (each CTA loads half of the tile's
+    B1 and B2 rows, the MMA thread copies the scale atoms into TMEM): task
+    shapes, M and N ragged against the 256-row pair blocks and the tile width
+    (the second CTA's B rows wholly past N at N = 8), batched L, and 64-wide
+    tiles in the upper half of a 128-row scale block."""
+    monkeypatch.setenv("NVFP4_DUAL_KERNEL", "paircp")
+    monkeypatch.setenv("NVFP4_DUAL_BN", bn)
+    data = I.generate_dual_input(m, n, k, l, seed=5 + m + n + k, device="cuda")
+    assert_close(run_dual(data), oracle_dual(data), f"dual paircp{bn} {m}x{n}x{k}x{l}")
+
+
 @pytest.mark.parametrize("m,n,k", [(512, 960, 1024), (300, 200, 2048), (256, 96, 256), (768, 2304, 512)])
 def test_dual_pair96_tile_edges(m, n, k, monkeypatch):
     """CTA-pair kernel with 96-column tiles: scale rows gathered across two
