@@ -105,8 +105,7 @@ struct Knobs {
   int dual_group_m = 32;   // NVFP4_DUAL_GROUP_M (measured: 16 -> 32 saves ~1.5% on 8192x14336x4096)
   int dual_splits = 0;     // NVFP4_DUAL_SPLITS (0 = automatic)
   int dual_bn = 0;         // NVFP4_DUAL_BN (64 / 128, or 64 / 96 / 128 for the pair kernel; 0 = automatic)
-  int dual_kernel = 0;     // NVFP4_DUAL_KERNEL: 0 automatic, 1 pair (CTA-pair kernel), 2 single,
-                           // 3 paircp (CTA-pair kernel, scale-copy mode)
+  int dual_kernel = 0;     // NVFP4_DUAL_KERNEL: 0 automatic, 1 pair (CTA-pair kernel), 2 single
   int dual_cluster = 0;    // NVFP4_DUAL_CLUSTER: 0 automatic, 1 off, 2 / 4 forced cluster split-K
   int grouped_bn = 0;      // NVFP4_GROUPED_BN (128 / 256; 0 = automatic)
   bool pdl = true;         // NVFP4_PDL=0: launch the GEMMs without programmatic dependent launch
@@ -127,10 +126,7 @@ Knobs read_knobs() {
     else if ((x = val("DUAL_SPLITS"))) k.dual_splits = atoi(x);
     else if ((x = val("DUAL_BN"))) k.dual_bn = atoi(x);
     else if ((x = val("DUAL_KERNEL")))
-      k.dual_kernel = strcmp(x, "pair") == 0     ? 1
-                      : strcmp(x, "single") == 0 ? 2
-                      : strcmp(x, "paircp") == 0 ? 3
-                                                 : 0;
+      k.dual_kernel = strcmp(x, "pair") == 0 ? 1 : strcmp(x, "single") == 0 ? 2 : 0;
     else if ((x = val("DUAL_CLUSTER"))) k.dual_cluster = atoi(x);
     else if ((x = val("GROUPED_BN"))) k.grouped_bn = atoi(x);
     else if ((x = val("PDL"))) k.pdl = atoi(x) != 0;
@@ -529,25 +525,22 @@ int launch_dual(DeviceState* d, int slot, DualParams& p, int forced_splits, int 
                      "dual_gemm_kernel");
 }
 
-// CTA-pair kernel: kBN-column tiles (128, 96 or 64), M=256 MMAs, one
-// accumulator; scales staged by warps, or (kCp) copied by the MMA thread.
-template <int kBN, int kStages, bool kCp = false>
+// CTA-pair kernel: kBN-column tiles (128 or 64), two M=256 x N=kBN MMAs per
+// 64-deep K step, one accumulator, scale atoms copied into TMEM by the MMA thread.
+template <int kBN, int kStages>
 int launch_dual_2sm(DeviceState* d, int slot, const void* a, const void* b1, const void* b2,
                     const void* sfa, const void* sfb1, const void* sfb2, void* c, int m, int n,
                     int k, int l, int group_m, const DualAlloc& al, cudaStream_t stream) {
-  using Cfg = Dual2smCfg<kBN, kStages, kCp>;
-  auto kern = dual_gemm_2sm_kernel<kBN, kStages, kCp>;
+  using Cfg = Dual2smCfg<kBN, kStages>;
+  auto kern = dual_gemm_2sm_kernel<kBN, kStages>;
   int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
   if (rc) return rc;
   Dual2smParams p;
   memset(&p, 0, sizeof(p));
-  p.sfa = static_cast<const uint8_t*>(sfa);
-  p.sfb1 = static_cast<const uint8_t*>(sfb1);
-  p.sfb2 = static_cast<const uint8_t*>(sfb2);
   p.c = static_cast<__half*>(c);
   p.m = m, p.n = n, p.k = k, p.l = l;
   p.mp_blocks = (m + 2 * kBM - 1) / (2 * kBM);
-  p.n_blocks = (n + Cfg::kBN - 1) / Cfg::kBN;
+  p.n_blocks = (n + kBN - 1) / kBN;
   p.k_blocks = k / kBK;
   p.tiles = l * p.mp_blocks * p.n_blocks;
   p.sfa_blocks = (m + 127) / 128;
@@ -556,20 +549,18 @@ int launch_dual_2sm(DeviceState* d, int slot, const void* a, const void* b1, con
   p.c_lines32 = (n % 16 == 0) && (reinterpret_cast<uintptr_t>(c) % 32 == 0);
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
-  const int b_box = kCp ? kBN / 2 : kBN;   // scale-copy mode: each CTA loads half of B1 and of B2
+  // each CTA loads half of the tile's B1 rows and half of its B2 rows
   if ((rc = encode_dual_operand(al, &p.tmap_a, a, m, k, l, kBM))) return rc;
-  if ((rc = encode_dual_operand(al, &p.tmap_b1, b1, n, k, l, b_box))) return rc;
-  if ((rc = encode_dual_operand(al, &p.tmap_b2, b2, n, k, l, b_box))) return rc;
-  if (kCp) {
-    const int rest_k = k / kKStep;
-    const int a_atoms = l * p.sfa_blocks * rest_k, b_atoms = l * p.sfb_blocks * rest_k;
-    auto enc = [&](CUtensorMap* map, const void* base, int atoms) {
-      return al.fixed ? encode_sf_atoms_uncached(map, base, atoms) : encode_sf_atoms(map, base, atoms);
-    };
-    if ((rc = enc(&p.tmap_sfa, sfa, a_atoms))) return rc;
-    if ((rc = enc(&p.tmap_sfb1, sfb1, b_atoms))) return rc;
-    if ((rc = enc(&p.tmap_sfb2, sfb2, b_atoms))) return rc;
-  }
+  if ((rc = encode_dual_operand(al, &p.tmap_b1, b1, n, k, l, kBN / 2))) return rc;
+  if ((rc = encode_dual_operand(al, &p.tmap_b2, b2, n, k, l, kBN / 2))) return rc;
+  const int rest_k = k / kKStep;
+  const int a_atoms = l * p.sfa_blocks * rest_k, b_atoms = l * p.sfb_blocks * rest_k;
+  auto enc = [&](CUtensorMap* map, const void* base, int atoms) {
+    return al.fixed ? encode_sf_atoms_uncached(map, base, atoms) : encode_sf_atoms(map, base, atoms);
+  };
+  if ((rc = enc(&p.tmap_sfa, sfa, a_atoms))) return rc;
+  if ((rc = enc(&p.tmap_sfb1, sfb1, b_atoms))) return rc;
+  if ((rc = enc(&p.tmap_sfb2, sfb2, b_atoms))) return rc;
   const int pairs = p.tiles < d->num_sms / 2 ? p.tiles : d->num_sms / 2;
   return launch_gemm(kern, (unsigned)(2 * pairs), Cfg::kThreads, Cfg::kSmemBytes, stream, p, 0,
                      "dual_gemm_2sm_kernel");
@@ -698,48 +689,34 @@ int run_dual(DeviceState* d, const void* a, const void* b1, const void* b2, cons
   p.group_m = kn.dual_group_m;
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
-  // Kernel choice: the single-CTA kernel (128-wide tiles; cluster split-K
-  // when the tiles leave SMs idle; 64-wide tiles on request), or the CTA-pair
-  // kernel (NVFP4_DUAL_KERNEL=pair; 96-wide tiles with NVFP4_DUAL_BN=96),
-  // which loads a third fewer operand bytes per SM but measures ~3% slower
-  // on configuration 1 (440 vs 428 us).  Automatic choice of the pair, for
-  // 12 to 32 K blocks (fewer favour the single kernel's shorter pipeline
-  // fill, more its K split), from the reference's benchmark shapes timed as
-  // its harness times them (us, pair vs single-CTA kernel):
-  //   one 256-row pair block (128 < M <= 256) where the single kernel would
-  //   leave SMs idle: 64-wide pair tiles when they make 64..num_sms CTAs
-  //   (256x4096x7168 17.2 / 18.8, 256x3072x4096 12.3 / 12.6, 256x2048x7168
-  //   16.2 / 17.1), else 128-wide when those make 48..num_sms CTAs;
-  //   two pair blocks (256 < M <= 512), when the 128-wide pair tiles fit one
-  //   wave (512x4096x7168 18.7 / 19.3, 512x3072x7168 18.5 / 19.0,
-  //   384x4096x7168 18.6 / 19.2);
-  //   otherwise single (256x7168x2048, 8 K blocks: 10.8 / 10.4;
-  //   256x512x1024: 7.0 / 6.9).
+  // Kernel choice: the CTA-pair kernel unless the single-CTA kernel's K
+  // split pays.  Measured on one B200 (us per call, 15 distinct inputs back
+  // to back after an L2 flush; pair 64-wide / pair 128-wide / single):
+  //   pair 64-wide tiles when they make at most one CTA per SM:
+  //     256x4096x7168 14.3 / 16.1 / 18.7, 256x3072x4096 10.2 / 11.6 / 12.3,
+  //     256x2048x7168 12.2 / 15.1 / 17.1, 256x4096x14336 22.8 / 25.5 / 25.5,
+  //     128x4096x7168 15.3 / 15.9 / 18.7, 256x512x1024 6.1 / 7.2 / 6.8;
+  //   otherwise the single-CTA kernel when it would split K (few tiles, at
+  //     least 48 K blocks) and the 128-wide pair tiles leave SMs idle:
+  //     128x7168x16384 (configuration 2) 38.3 pair 128-wide / 36.8 single;
+  //   otherwise pair 128-wide tiles: 512x4096x7168 21.8 / 16.9 / 18.9,
+  //     512x7168x2048 17.0 / 14.1 / 15.2, 1024x4096x7168 36.8 / 27.2 / 33.0,
+  //     2048x4096x7168 62.4 / 48.6 / 60.2, 256x7168x2048 11.7 / 10.1 / 11.3,
+  //     8192x14336x4096 (configuration 1) 507 / 352 / 427.
+  // NVFP4_DUAL_KERNEL=pair|single forces the kernel (NVFP4_DUAL_BN=64|128 its
+  // tile width; NVFP4_DUAL_BN alone: the single-CTA kernel at that width).
+  const int pair_blocks = l * ((m + 2 * kBM - 1) / (2 * kBM));
+  const int ctas64 = 2 * pair_blocks * ((n + 63) / 64);
+  const int ctas128 = 2 * pair_blocks * ((n + 127) / 128);
+  const bool forced_single = kn.dual_kernel == 2 || kn.dual_splits > 0 || kn.dual_cluster > 0;
   bool pair = kn.dual_kernel == 1;
-  int pair_bn = kn.dual_bn;
-  if (kn.dual_kernel == 0 && kn.dual_bn == 0 && kn.dual_splits == 0 && kn.dual_cluster == 0 &&
-      p.k_blocks >= 12 && p.k_blocks <= 32) {
-    const int single_tiles = l * ((m + kBM - 1) / kBM) * ((n + 127) / 128);
-    const int ctas128 = 2 * l * ((m + 2 * kBM - 1) / (2 * kBM)) * ((n + 127) / 128);
-    const int ctas64 = 2 * l * ((m + 2 * kBM - 1) / (2 * kBM)) * ((n + 63) / 64);
-    if (m > 128 && m <= 256 && single_tiles < d->num_sms) {
-      if (ctas64 >= 64 && ctas64 <= d->num_sms) pair = true, pair_bn = 64;
-      else if (ctas128 >= 48 && ctas128 <= d->num_sms) pair = true, pair_bn = 128;
-    } else if (m > 256 && m <= 512 && ctas128 >= 48 && ctas128 <= d->num_sms) {
-      pair = true, pair_bn = 128;
-    }
-  }
-  if (kn.dual_kernel == 3) {
-    if (pair_bn == 128)
-      return launch_dual_2sm<128, 5, true>(d, 17, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
-                                           kn.dual_group_m, al, stream);
-    return launch_dual_2sm<64, 7, true>(d, 16, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
-                                        kn.dual_group_m, al, stream);
+  int pair_bn = kn.dual_bn == 64 || kn.dual_bn == 128 ? kn.dual_bn : 0;
+  if (!pair && !forced_single && kn.dual_bn == 0) {
+    if (ctas64 <= d->num_sms) pair = true, pair_bn = 64;
+    else if (!(p.k_blocks >= 48 && ctas128 < d->num_sms)) pair = true, pair_bn = 128;
   }
   if (pair) {
-    if (pair_bn == 96)
-      return launch_dual_2sm<96, 5>(d, 3, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
-                                    kn.dual_group_m, al, stream);
+    if (pair_bn == 0) pair_bn = ctas64 <= d->num_sms ? 64 : 128;
     if (pair_bn == 64)
       return launch_dual_2sm<64, 7>(d, 15, a, b1, b2, sfa, sfb1, sfb2, c, m, n, k, l,
                                     kn.dual_group_m, al, stream);

@@ -6,36 +6,37 @@
 // (nvfp4_dual_gemm/reference.py:27-77); own design:
 //
 // * a CTA pair (cluster of 2 on neighbouring SMs) owns a 256 x kBN tile of C
-//   (kBN = 128, 96 or 64).  CTA r holds A rows [256*mp + 128*r, +128) and one
-//   kBN-row B tile: CTA 0 the B1 rows of the tile's columns, CTA 1 the B2
-//   rows.  One tcgen05.mma.cta_group::2 with M = 256, N = 2*kBN per 64-deep
-//   K step then writes, in each CTA's TMEM, its 128 rows x [gate kBN | up
-//   kBN].  Per SM and K step: A 16 KB + B kBN/8 KB of operands for 128 x kBN
-//   outputs (the single-CTA kernel: 48 KB for 128 x 128 outputs), and one
-//   MMA instruction covers both SMs.  64-wide tiles put twice as many pairs
-//   on a shape with few 256-row blocks (e.g. M = 256, N = 4096: 128 CTAs
-//   instead of 64) at 30 KB per SM and K step;
+//   (kBN = 128 or 64).  CTA r holds A rows [256*mp + 128*r, +128) and half
+//   of the tile's B1 rows and half of its B2 rows (rows [n0 + r*kBN/2,
+//   +kBN/2) of each).  Per 64-deep K step two tcgen05.mma.cta_group::2 with
+//   M = 256, N = kBN (whose B operand is split half per CTA) write gate and
+//   up into each CTA's TMEM: its 128 rows x [gate kBN | up kBN].  The second
+//   MMA takes A from the tensor core's collector buffer, where the first left
+//   it, so A is read from shared memory once.  Per SM and 256-deep K block:
+//   A 16 KB + B kBN/8 KB for 128 x kBN outputs (the single-CTA kernel: 48 KB
+//   for 128 x 128);
+// * scale factors: each CTA loads its 4 SFA atoms and the 4 SFB1 and 4 SFB2
+//   atoms of the tile's 128-row block per K block by TMA, onto the same
+//   leader stage barrier as the tiles.  The MMA thread copies them into TMEM
+//   itself (tcgen05.cp.cta_group::2.32x128b.warpx4, one instruction per atom
+//   and pair: row i of the atom to lane i of every lane quadrant of both
+//   CTAs, 4 columns) right before the MMAs that read them; the tensor pipe
+//   runs one thread's copies and MMAs in issue order.  A 64-wide tile reads
+//   columns (n0 % 128) / 32 + {0, 1} of the B atoms.  Each pipeline stage
+//   owns one TMEM scale buffer (48 columns);
 // * one accumulator; eight epilogue warps per CTA pull their gate and up
 //   columns into registers and release the accumulator (remote arrives on
 //   the leader's barrier) before the math and the stores;
-// * scale factors: each CTA bulk-loads its A atoms and the B1 / B2 atom
-//   blocks covering the tile onto a landing barrier; four staging warps per
-//   CTA write them into TMEM with tcgen05.st (SFA: 4 columns per K step;
-//   SFB: column 8j + c holds B rows 32c..32c+31 of the 2*kBN-row operand,
-//   whole atom rows for 128-wide tiles, gathered 4-byte columns for 96- and
-//   64-wide ones) and arrive on the leader's per-stage barrier.  Each pipeline stage
-//   owns one TMEM scale buffer: refilling a stage already waits for the
-//   MMAs that read it;
-// * each CTA issues its copies from two threads in parallel, one for the
-//   operand tiles and one for the scale atoms (a single thread issuing both
-//   measured ~840 cycles per K step, slower than the MMAs of a 64-wide tile);
-//   both CTAs count their tile bytes on the leader's stage barrier
-//   (TMA .cta_group::2, no multicast); the leader commits to both CTAs
+// * each CTA issues its copies from two threads in parallel (operand tiles;
+//   scale atoms), both counting on the leader's stage barrier (TMA
+//   .cta_group::2, no multicast); the leader commits to both CTAs
 //   (tcgen05.commit multicast); cross-CTA handshakes use CTA-scope-release
-//   remote arrives; cluster barriers bracket setup and teardown.  All waits
-//   are bounded.  The second CTA of the last pair block may lie wholly past
-//   M: its A rows load as zeros, it stores nothing, and it re-reads the last
-//   real A-scale block.
+//   remote arrives; cluster barriers bracket setup and teardown.  The
+//   issuing threads are chosen with elect.sync and the MMA thread advances
+//   precomputed descriptors: both keep its per-instruction cost low, which
+//   sets the pace of small tiles.  All waits are bounded.  The second CTA of
+//   the last pair block may lie wholly past M: its A rows load as zeros, it
+//   stores nothing, and it re-reads the last real A-scale block.
 #pragma once
 #include <cuda.h>
 #include "kernel_common.cuh"
@@ -44,14 +45,11 @@ namespace nvfp4 {
 
 struct Dual2smParams {
   CUtensorMap tmap_a;    // bytes [L][M][K/2], box {128 B, 128 rows, 1}
-  CUtensorMap tmap_b1;   // bytes [L][N][K/2], box {128 B, kBN rows, 1}
+  CUtensorMap tmap_b1;   // bytes [L][N][K/2], box {128 B, kBN/2 rows, 1}
   CUtensorMap tmap_b2;
-  // scale-copy mode only: the scale atoms as 2-D [atoms][128 x 32-bit] maps,
-  // box {128, 4} (one 256-deep K step of one 128-row block)
+  // scale atoms as 2-D [atoms][128 x 32-bit] maps, box {128, 4}: the four
+  // atoms of one 256-deep K block of one 128-row block
   CUtensorMap tmap_sfa, tmap_sfb1, tmap_sfb2;
-  const uint8_t* sfa;    // permuted scale atoms [L][ceil(M/128)][K/64][512]
-  const uint8_t* sfb1;   // [L][ceil(N/128)][K/64][512]
-  const uint8_t* sfb2;
   __half* c;             // [L][M][N]
   int m, n, k, l;
   int mp_blocks, n_blocks, k_blocks, tiles;  // 256-row pair blocks, kBN-column blocks
@@ -62,44 +60,30 @@ struct Dual2smParams {
   long long wait_limit;
 };
 
-template <int kBN_, int kStages, bool kCp_ = false>
+template <int kBN_, int kStages>
 struct Dual2smCfg {
-  static constexpr int kBN = kBN_;                     // C columns per tile: 64, 96 or 128
-  // scale-copy mode: each CTA loads half of the tile's B1 rows and half of
-  // its B2 rows, the scale atoms arrive by TMA on the stage barrier, and the
-  // MMA thread copies them into TMEM itself (tcgen05.cp) before two MMAs
-  // (gate, up) of N = kBN per K step; no staging warps
-  static constexpr bool kCp = kCp_;
-  static constexpr int kNmma = kCp ? kBN : 2 * kBN;    // pair MMA N: [B1 tile ; B2 tile], or one of them
-  static constexpr int kBHalfBytes = (kBN / 2) * kBK / 2;   // scale-copy mode: B1 or B2 rows of one CTA
-  static constexpr int kGroups = kBN / 32;             // 32-row groups per B tile
-  static constexpr int kSfbBlocks = kBN == 96 ? 2 : 1;    // 128-row atom blocks covering a tile
+  static constexpr int kBN = kBN_;                     // C columns per tile: 64 or 128
   static constexpr int kABytes = kBM * kBK / 2;        // 16 KB
-  static constexpr int kBBytes = kBN * kBK / 2;        // 8, 12 or 16 KB
+  static constexpr int kBHalfBytes = (kBN / 2) * kBK / 2;   // this CTA's B1 (or B2) rows: 4 or 8 KB
+  static constexpr int kBBytes = 2 * kBHalfBytes;      // B1 half, then B2 half
   static constexpr int kSfaBytes = kSfStageBytes;      // 4 atoms of this CTA's A rows
-  static constexpr int kSfbBytes = kSfbBlocks * kSfStageBytes;   // per B operand
-  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + 2 * kSfbBytes;   // 30-38 KB
-  // bytes both CTAs' copies of a stage count on the leader's stage barrier
-  static constexpr int kPairTxBytes = kCp ? 2 * (kABytes + kBBytes + kSfaBytes + 2 * kSfbBytes)
-                                          : 2 * (kABytes + kBBytes);
+  static constexpr int kSfbBytes = kSfStageBytes;      // 4 atoms of the tile's B1 (or B2) block
+  static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + 2 * kSfbBytes;   // 30 or 38 KB
+  static constexpr int kPairTxBytes = 2 * kStageBytes;  // both CTAs' copies of a stage
   static constexpr int kEpiWarps = 8;                   // 2 per TMEM quadrant
-  static constexpr int kColsPerWarp = kBN / 2;         // 32, 48 or 64 columns of gate and of up
-  static constexpr int kSfWarps = kCp ? 0 : 4;
-  // warp roles: epilogue [0, 8), tile producer 8, MMA 9, scale producer 10,
-  // scale staging [11, 15)
-  static constexpr int kProdWarp = kEpiWarps, kMmaWarp = kEpiWarps + 1;
-  static constexpr int kSfProdWarp = kEpiWarps + 2, kSfWarp0 = kEpiWarps + 3;
-  static constexpr int kThreads = 32 * (kEpiWarps + 3 + kSfWarps);
+  static constexpr int kColsPerWarp = kBN / 2;         // 32 or 64 columns of gate and of up
+  // warp roles: epilogue [0, 8), tile producer 8, MMA 9, scale producer 10
+  static constexpr int kProdWarp = kEpiWarps, kMmaWarp = kEpiWarps + 1, kSfProdWarp = kEpiWarps + 2;
+  static constexpr int kThreads = 32 * (kEpiWarps + 3);
   static constexpr int kSmemBytes = kStages * kStageBytes + 1024;
   static constexpr int kTmemCols = 512;
   static constexpr int kAccBufs = 1;
   static constexpr int kAccCols = 2 * kBN;             // gate columns, then up columns
-  static constexpr int kSfCol = kAccBufs * kAccCols;   // 2 * kBN
-  static constexpr int kSfBufCols = 48;                // per stage: SFA 4x4 + SFB 4x8 (6 used)
+  static constexpr int kSfCol = kAccBufs * kAccCols;
+  static constexpr int kSfBufCols = 48;                // per stage: SFA, SFB1, SFB2 x 4 atoms x 4 columns
   static_assert(kStageBytes % 1024 == 0, "stages must stay 1024-byte aligned");
   static_assert(kSfCol + kStages * kSfBufCols <= kTmemCols, "TMEM budget: one scale buffer per stage");
-  static_assert(kBN == 64 || kBN == 96 || kBN == 128, "tile width");
-  static_assert(!kCp || kBN != 96, "scale-copy mode: a tile lies in one 128-row scale block");
+  static_assert(kBN == 64 || kBN == 128, "tile width: a tile lies in one 128-row scale block");
 };
 
 struct PairTile2 { int l, mp, nb; };
@@ -119,13 +103,12 @@ __device__ __forceinline__ PairTile2 pair2_tile_coord(const Dual2smParams& p, in
   return tc;
 }
 
-template <int kBN, int kStages, bool kCp>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Dual2smCfg<kBN, kStages, kCp>::kThreads, 1)
+template <int kBN, int kStages>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(Dual2smCfg<kBN, kStages>::kThreads, 1)
 dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
-  using Cfg = Dual2smCfg<kBN, kStages, kCp>;
+  using Cfg = Dual2smCfg<kBN, kStages>;
   extern __shared__ uint8_t smem_raw[];
   __shared__ uint64_t bar_full[kStages], bar_empty[kStages];
-  __shared__ uint64_t bar_sf_landed[kStages];
   __shared__ uint64_t bar_acc_full[Cfg::kAccBufs], bar_acc_empty[Cfg::kAccBufs];
   __shared__ uint64_t bar_drain;
   __shared__ uint32_t s_tmem_base;
@@ -140,11 +123,9 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
-      // the leader's expect_tx arrival + one per staging warp of both CTAs (+ the
-      // TMA bytes of both CTAs)
-      mbar_init(smem_u32(&bar_full[s]), 1 + 2 * Cfg::kSfWarps);   // (scale-copy mode: 1)
+      // the leader's expect_tx arrival (+ the copy bytes of both CTAs)
+      mbar_init(smem_u32(&bar_full[s]), 1);
       mbar_init(smem_u32(&bar_empty[s]), 1);
-      mbar_init(smem_u32(&bar_sf_landed[s]), 1);
     }
     for (int b = 0; b < Cfg::kAccBufs; ++b) {
       mbar_init(smem_u32(&bar_acc_full[b]), 1);
@@ -157,15 +138,11 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
   }
   if (warp == Cfg::kProdWarp && lane == 0) {
     tma_prefetch_desc(&p.tmap_a);
-    if constexpr (kCp) {
-      tma_prefetch_desc(&p.tmap_b1);
-      tma_prefetch_desc(&p.tmap_b2);
-      tma_prefetch_desc(&p.tmap_sfa);
-      tma_prefetch_desc(&p.tmap_sfb1);
-      tma_prefetch_desc(&p.tmap_sfb2);
-    } else {
-      tma_prefetch_desc(rank == 0 ? &p.tmap_b1 : &p.tmap_b2);
-    }
+    tma_prefetch_desc(&p.tmap_b1);
+    tma_prefetch_desc(&p.tmap_b2);
+    tma_prefetch_desc(&p.tmap_sfa);
+    tma_prefetch_desc(&p.tmap_sfb1);
+    tma_prefetch_desc(&p.tmap_sfb2);
   }
   if (warp == Cfg::kMmaWarp) tmem_alloc_pair<Cfg::kTmemCols>(smem_u32(&s_tmem_base));
   tc_fence_before();
@@ -182,18 +159,14 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
   if (warp == Cfg::kProdWarp || warp == Cfg::kSfProdWarp) {
     // ------------------------------------------------------------ TMA producers (both CTAs)
     // Two threads issue each stage's copies in parallel: warp kProdWarp the
-    // operand tiles (onto the leader's full barrier), warp kSfProdWarp the
-    // scale atoms (onto this CTA's landing barrier).  Every copy instruction
-    // and barrier operation costs its issuing thread ~60-100 cycles, so one
-    // thread issuing all of a stage (~840 cycles per 256-deep K step,
-    // measured) rather than the MMAs set the pace of the main loop.
-    // elect.sync rather than lane == 0: the compiler then knows one thread
-    // runs the region and keeps its addresses and descriptors in uniform
-    // registers, which the copy and MMA instructions take directly
+    // operand tiles, warp kSfProdWarp the scale atoms, all onto the leader's
+    // stage barrier (every copy instruction and barrier operation costs its
+    // issuing thread tens of cycles).  elect.sync rather than lane == 0: the
+    // compiler then knows one thread runs the region and keeps its addresses
+    // in uniform registers, which the copy instructions take directly.
     if (elect_one()) {
       const bool tile_role = warp == Cfg::kProdWarp;
       const uint64_t pol = policy_evict_normal();
-      const CUtensorMap* tmap_b = rank == 0 ? &p.tmap_b1 : &p.tmap_b2;
       int stage = 0;
       uint32_t phase = 0;
       // per stage: ever issued, and the phase of its last issue (abort drain)
@@ -202,19 +175,14 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
       for (int t = pair; t < p.tiles && ok; t += num_pairs) {
         const PairTile2 tc = pair2_tile_coord(p, t);
         const int m0 = tc.mp * 2 * kBM + (int)rank * kBM;   // this CTA's A rows
-        const int n0 = tc.nb * Cfg::kBN;
-        const int blk0 = n0 / 128;
-        const int blk1 = min(blk0 + 1, p.sfb_blocks - 1);   // past N: re-read the last block
-        const size_t atoms = (size_t)rest_k * kSfAtom;
+        const int n0 = tc.nb * kBN;
+        const int nb0 = n0 + (int)rank * (kBN / 2);         // this CTA's B1 / B2 rows
         // the second CTA of the last pair block may lie wholly past M (odd
         // ceil(M/128)): its A rows load as zeros, it stores nothing, and it
         // re-reads the last real scale block rather than reading past the tensor
         const int ablk = min(m0 / 128, p.sfa_blocks - 1);
-        const uint8_t* sfa_t = p.sfa + ((size_t)tc.l * p.sfa_blocks + ablk) * atoms;
-        const uint8_t* sfb1_0 = p.sfb1 + ((size_t)tc.l * p.sfb_blocks + blk0) * atoms;
-        const uint8_t* sfb1_1 = p.sfb1 + ((size_t)tc.l * p.sfb_blocks + blk1) * atoms;
-        const uint8_t* sfb2_0 = p.sfb2 + ((size_t)tc.l * p.sfb_blocks + blk0) * atoms;
-        const uint8_t* sfb2_1 = p.sfb2 + ((size_t)tc.l * p.sfb_blocks + blk1) * atoms;
+        const int a_atom0 = (tc.l * p.sfa_blocks + ablk) * rest_k;
+        const int b_atom0 = (tc.l * p.sfb_blocks + n0 / 128) * rest_k;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
           if (!ctl.wait(smem_u32(&bar_empty[stage]), phase ^ 1u, kDevTimeoutStageFree)) {
             ok = false;
@@ -222,70 +190,43 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
           }
           const uint32_t sa = smem_base + stage * Cfg::kStageBytes;
           const uint32_t sb = sa + Cfg::kABytes;
+          const uint32_t full = mapa_shared(smem_u32(&bar_full[stage]), 0);
           if (tile_role) {
-            // operand tiles: both CTAs' bytes complete on the leader's stage barrier
-            const uint32_t full = mapa_shared(smem_u32(&bar_full[stage]), 0);
             if (leader) mbar_arrive_expect_tx(smem_u32(&bar_full[stage]), Cfg::kPairTxBytes);
             tma_load_3d_pair(sa, &p.tmap_a, full, kb * 128, m0, tc.l, pol);
-            if constexpr (kCp) {
-              // this CTA's half of the tile's B1 rows, then of its B2 rows
-              const int nb0 = n0 + (int)rank * (kBN / 2);
-              tma_load_3d_pair(sb, &p.tmap_b1, full, kb * 128, nb0, tc.l, pol);
-              tma_load_3d_pair(sb + Cfg::kBHalfBytes, &p.tmap_b2, full, kb * 128, nb0, tc.l, pol);
-            } else {
-              tma_load_3d_pair(sb, tmap_b, full, kb * 128, n0, tc.l, pol);
-            }
-          } else if constexpr (kCp) {
-            // scale atoms [SFA][SFB1][SFB2] (4 atoms each), also counted on the
-            // leader's stage barrier: the MMA thread copies them to TMEM itself
-            const uint32_t ssf = sb + Cfg::kBBytes;
-            const uint32_t full = mapa_shared(smem_u32(&bar_full[stage]), 0);
-            const int ka = kb * (kBK / kKStep);
-            const int a_atom = (tc.l * p.sfa_blocks + ablk) * rest_k + ka;
-            const int b_atom = (tc.l * p.sfb_blocks + blk0) * rest_k + ka;
-            tma_load_2d_pair(ssf, &p.tmap_sfa, full, 0, a_atom, pol);
-            tma_load_2d_pair(ssf + Cfg::kSfaBytes, &p.tmap_sfb1, full, 0, b_atom, pol);
-            tma_load_2d_pair(ssf + Cfg::kSfaBytes + Cfg::kSfbBytes, &p.tmap_sfb2, full, 0, b_atom, pol);
+            tma_load_3d_pair(sb, &p.tmap_b1, full, kb * 128, nb0, tc.l, pol);
+            tma_load_3d_pair(sb + Cfg::kBHalfBytes, &p.tmap_b2, full, kb * 128, nb0, tc.l, pol);
           } else {
-            // scales, on this CTA's own landing barrier:
-            // [SFA][SFB1 block 0 (, 1)][SFB2 block 0 (, 1)]
+            // [SFA][SFB1][SFB2], 4 atoms each
             const uint32_t ssf = sb + Cfg::kBBytes;
-            const uint32_t landed = smem_u32(&bar_sf_landed[stage]);
-            mbar_arrive_expect_tx(landed, Cfg::kSfaBytes + 2 * Cfg::kSfbBytes);
-            const size_t so = (size_t)kb * kSfStageBytes;
-            const uint32_t sb1 = ssf + Cfg::kSfaBytes, sb2 = sb1 + Cfg::kSfbBytes;
-            bulk_load(ssf, sfa_t + so, kSfStageBytes, landed, pol);
-            bulk_load(sb1, sfb1_0 + so, kSfStageBytes, landed, pol);
-            bulk_load(sb2, sfb2_0 + so, kSfStageBytes, landed, pol);
-            if constexpr (Cfg::kSfbBlocks == 2) {
-              bulk_load(sb1 + kSfStageBytes, sfb1_1 + so, kSfStageBytes, landed, pol);
-              bulk_load(sb2 + kSfStageBytes, sfb2_1 + so, kSfStageBytes, landed, pol);
-            }
+            const int ka = kb * (kBK / kKStep);
+            tma_load_2d_pair(ssf, &p.tmap_sfa, full, 0, a_atom0 + ka, pol);
+            tma_load_2d_pair(ssf + Cfg::kSfaBytes, &p.tmap_sfb1, full, 0, b_atom0 + ka, pol);
+            tma_load_2d_pair(ssf + Cfg::kSfaBytes + Cfg::kSfbBytes, &p.tmap_sfb2, full, 0, b_atom0 + ka,
+                             pol);
           }
           issued |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
           if (++stage == kStages) stage = 0, phase ^= 1u;
         }
       }
-      if (!ok) {  // in-flight copies land before the CTA winds down
-        // (a peer's copies land on the leader's stage barriers: the leader
-        // drains them, and the closing cluster barrier holds the peer)
+      if (!ok && leader) {
+        // in-flight copies land before the CTA winds down (a peer's copies
+        // land on the leader's stage barriers: the leader drains them, and
+        // the closing cluster barrier holds the peer)
         for (int s = 0; s < kStages; ++s)
-          if ((issued >> s) & 1u) {
-            if (!tile_role && !kCp) ctl.drain(smem_u32(&bar_sf_landed[s]), (last_phase >> s) & 1u);
-            else if (leader) ctl.drain_copies(smem_u32(&bar_full[s]), (last_phase >> s) & 1u);
-          }
+          if ((issued >> s) & 1u) ctl.drain_copies(smem_u32(&bar_full[s]), (last_phase >> s) & 1u);
       }
     }
   } else if (warp == Cfg::kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (leader && elect_one()) {
-      constexpr uint32_t idesc = (1u << 7) | (1u << 10) | ((uint32_t)(Cfg::kNmma >> 3) << 17) |
-                                 ((uint32_t)(256 >> 4) << 24);   // M=256, N=2*kBN, e2m1 x e2m1, e4m3 scales
+      // M = 256, N = kBN, e2m1 x e2m1, e4m3 scales
+      constexpr uint32_t idesc = (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+                                 ((uint32_t)(256 >> 4) << 24);
       constexpr uint16_t kBoth = 0x3;
       const uint64_t a_desc0 = kmajor_sw128_desc(smem_base);   // stage 0's A tile
-      // stage 0's first SFA atom (scale-copy mode)
-      const uint64_t sf_desc0 = sf_atom_desc(smem_base + Cfg::kABytes + Cfg::kBBytes);
+      const uint64_t sf_desc0 = sf_atom_desc(smem_base + Cfg::kABytes + Cfg::kBBytes);   // its first SFA atom
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -298,14 +239,10 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
         }
         tc_fence_after();
         const uint32_t d_acc = tmem + acc * Cfg::kAccCols;
-        // scale-copy mode: the tile's B rows start at column (n0 % 128) / 32
-        // of their 128-row scale atoms
-        const uint32_t b_col = kCp ? (uint32_t)((pair2_tile_coord(p, t).nb * kBN) % 128) / 32u : 0u;
+        // the tile's B rows start at column (n0 % 128) / 32 of their scale atoms
+        const uint32_t b_col = (uint32_t)((pair2_tile_coord(p, t).nb * kBN) % 128) / 32u;
         for (int kb = 0; kb < p.k_blocks; ++kb) {
-          // both CTAs' operand tiles landed and scales staged: one barrier
-          // counts all of it, so this thread checks one barrier per K step
-          // (each check costs it ~100 cycles, and its loop sets the pace of
-          // small tiles)
+          // both CTAs' tiles and scale atoms landed: one barrier counts it all
           if (!ctl.wait(smem_u32(&bar_full[stage]), phase, kDevTimeoutTmaFull)) {
             ok = false;
             break;
@@ -314,34 +251,24 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
           // descriptors of this stage's tiles and atoms: the stage-0 ones advanced
           const uint32_t so = (uint32_t)stage * Cfg::kStageBytes;
           const uint64_t da = desc_advance(a_desc0, so);
-          const uint64_t db = desc_advance(da, Cfg::kABytes);   // this CTA's B rows
+          const uint64_t db = desc_advance(da, Cfg::kABytes);   // this CTA's B1 rows, then B2 rows
+          const uint64_t dsf = desc_advance(sf_desc0, so);
           const uint32_t sf_a = tmem + Cfg::kSfCol + stage * Cfg::kSfBufCols;
-          const uint32_t sf_b = sf_a + 16;
-          if constexpr (kCp) {
-            // per 64-deep step: the step's SFA, SFB1 and SFB2 atoms into TMEM
-            // (columns sf_a + 4j, sf_b + 4j, sf_b + 16 + 4j), then gate and up
-            // (A kept in the collector between them); the tensor pipe runs
-            // this thread's copies and MMAs in issue order
-            const uint64_t dsf = desc_advance(sf_desc0, so);
-            #pragma unroll
-            for (int j = 0; j < kBK / kKStep; ++j) {
-              const uint64_t dsa = desc_advance(dsf, j * kSfAtom);
-              tc_cp_pair_32x128b_x4(sf_a + 4 * j, dsa);
-              tc_cp_pair_32x128b_x4(sf_b + 4 * j, desc_advance(dsa, Cfg::kSfaBytes));
-              tc_cp_pair_32x128b_x4(sf_b + 16 + 4 * j, desc_advance(dsa, Cfg::kSfaBytes + Cfg::kSfbBytes));
-              const uint64_t daj = desc_advance(da, 32 * j), db1 = desc_advance(db, 32 * j);
-              const uint32_t acc_in = (kb | j) != 0;
-              tc_mma_nvf4_pair_ca<CollectorA::kFill>(d_acc, daj, db1, idesc, sf_a + 4 * j,
-                                                    sf_b + 4 * j + b_col, acc_in);
-              tc_mma_nvf4_pair_ca<CollectorA::kLastUse>(d_acc + kBN, daj,
-                                                       desc_advance(db1, Cfg::kBHalfBytes), idesc,
-                                                       sf_a + 4 * j, sf_b + 16 + 4 * j + b_col, acc_in);
-            }
-          } else {
-            #pragma unroll
-            for (int j = 0; j < kBK / kKStep; ++j)
-              tc_mma_nvf4_pair(d_acc, desc_advance(da, 32 * j), desc_advance(db, 32 * j), idesc,
-                               sf_a + 4 * j, sf_b + 8 * j, (kb | j) != 0);
+          const uint32_t sf_b1 = sf_a + 16, sf_b2 = sf_a + 32;
+          // per 64-deep step j: its SFA, SFB1 and SFB2 atoms into TMEM
+          // (columns [4j, +4) of each 16-column part), then gate and up
+          #pragma unroll
+          for (int j = 0; j < kBK / kKStep; ++j) {
+            const uint64_t dsa = desc_advance(dsf, j * kSfAtom);
+            tc_cp_pair_32x128b_x4(sf_a + 4 * j, dsa);
+            tc_cp_pair_32x128b_x4(sf_b1 + 4 * j, desc_advance(dsa, Cfg::kSfaBytes));
+            tc_cp_pair_32x128b_x4(sf_b2 + 4 * j, desc_advance(dsa, Cfg::kSfaBytes + Cfg::kSfbBytes));
+            const uint64_t daj = desc_advance(da, 32 * j), db1 = desc_advance(db, 32 * j);
+            const uint32_t acc_in = (kb | j) != 0;
+            tc_mma_nvf4_pair_ca<CollectorA::kFill>(d_acc, daj, db1, idesc, sf_a + 4 * j,
+                                                  sf_b1 + 4 * j + b_col, acc_in);
+            tc_mma_nvf4_pair_ca<CollectorA::kLastUse>(d_acc + kBN, daj, desc_advance(db1, Cfg::kBHalfBytes),
+                                                     idesc, sf_a + 4 * j, sf_b2 + 4 * j + b_col, acc_in);
           }
           tc_commit_pair(smem_u32(&bar_empty[stage]), kBoth);   // stage (and scale buffer) free
           any = true;
@@ -354,75 +281,6 @@ dual_gemm_2sm_kernel(const __grid_constant__ Dual2smParams p) {
       if (!ok && any) {
         tc_commit_pair(smem_u32(&bar_drain), 0x1);
         ctl.drain(smem_u32(&bar_drain), 0);
-      }
-    }
-  } else if (!kCp && warp >= Cfg::kSfWarp0) {
-    // ------------------------------------------------------------ scale staging (both CTAs)
-    // Warp w writes TMEM lanes [32*(w%4), +32) of its own CTA.  Lane i of every
-    // quadrant receives row i of each atom column the MMA reads: SFA atom j in
-    // columns [4j, +4) (this CTA's 128 A rows); SFB column 8j + c,
-    // c < 2 * kGroups, the scales of B rows 32c + i of the 2*kBN-row operand
-    // (c < kGroups: B1 tile rows, then B2 tile rows), gathered from the
-    // 128-row atom blocks (128-wide tiles: whole atom rows).
-    const uint32_t t_quad = ((uint32_t)(warp & 3) * 32u) << 16;
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true;
-    for (int t = pair; t < p.tiles && ok; t += num_pairs) {
-      const PairTile2 tc = pair2_tile_coord(p, t);
-      const int n0 = tc.nb * Cfg::kBN;
-      const int blk0 = n0 / 128;
-      // for row group c' of a B tile: which loaded atom block, and which
-      // 4-byte column of the atom row
-      uint32_t off[Cfg::kGroups];
-      #pragma unroll
-      for (int c = 0; c < Cfg::kGroups; ++c) {
-        const int r = n0 + 32 * c;
-        off[c] = (uint32_t)((r / 128 - blk0) * kSfStageBytes + ((r / 32) & 3) * 4);
-      }
-      for (int kb = 0; kb < p.k_blocks; ++kb) {
-        // the stage's scales landed (its refill already waited for the MMAs
-        // that read this stage's scale buffer)
-        bool got = true;
-        if (lane == 0) got = ctl.wait(smem_u32(&bar_sf_landed[stage]), phase, kDevTimeoutTmaFull);
-        if (!__shfl_sync(0xffffffffu, got ? 1 : 0, 0)) {
-          ok = false;
-          break;
-        }
-        mbar_try_wait(smem_u32(&bar_sf_landed[stage]), phase);   // every lane observes the phase
-        tc_fence_after();
-        const uint32_t ssf = smem_base + stage * Cfg::kStageBytes + Cfg::kABytes + Cfg::kBBytes;
-        const uint32_t row = lane * 16u;
-        uint32_t ra[16], rb[32];
-        #pragma unroll
-        for (int j = 0; j < kBK / kKStep; ++j) {
-          const uint4 a = lds_v4(ssf + j * kSfAtom + row);
-          ra[4 * j + 0] = a.x, ra[4 * j + 1] = a.y, ra[4 * j + 2] = a.z, ra[4 * j + 3] = a.w;
-          if constexpr (Cfg::kBN == 128) {
-            // the tile is one whole atom block of B1 and of B2: atom rows as they are
-            const uint4 b1 = lds_v4(ssf + Cfg::kSfaBytes + j * kSfAtom + row);
-            const uint4 b2 = lds_v4(ssf + Cfg::kSfaBytes + Cfg::kSfbBytes + j * kSfAtom + row);
-            rb[8 * j + 0] = b1.x, rb[8 * j + 1] = b1.y, rb[8 * j + 2] = b1.z, rb[8 * j + 3] = b1.w;
-            rb[8 * j + 4] = b2.x, rb[8 * j + 5] = b2.y, rb[8 * j + 6] = b2.z, rb[8 * j + 7] = b2.w;
-          } else {
-            #pragma unroll
-            for (int c = 0; c < 2 * Cfg::kGroups; ++c) {
-              const int op = c / Cfg::kGroups;   // 0: B1 rows, 1: B2 rows
-              const uint32_t base = ssf + Cfg::kSfaBytes + op * Cfg::kSfbBytes;
-              rb[8 * j + c] = lds_u32(base + off[c % Cfg::kGroups] + j * kSfAtom + row);
-            }
-            #pragma unroll
-            for (int c = 2 * Cfg::kGroups; c < 8; ++c) rb[8 * j + c] = 0u;
-          }
-        }
-        const uint32_t t_buf = tmem + t_quad + Cfg::kSfCol + stage * Cfg::kSfBufCols;
-        tmem_st_32x32b_x16(t_buf, ra);
-        tmem_st_32x32b_x32(t_buf + 16, rb);
-        tmem_st_wait();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive_remote(mapa_shared(smem_u32(&bar_full[stage]), 0));
-        if (++stage == kStages) stage = 0, phase ^= 1u;
       }
     }
   } else {

@@ -72,56 +72,32 @@ def run_dual(data):
     return out.cpu().numpy()
 
 
-@pytest.mark.parametrize("kernel", ["auto", "pair", "pair96"])
+@pytest.mark.parametrize("kernel", ["auto", "pair64", "pair128", "single"])
 @pytest.mark.parametrize("m,n,k,l", DUAL_TASK_TESTS)
 def test_dual_task_shapes(m, n, k, l, kernel, monkeypatch):
-    if kernel != "auto":
+    if kernel == "single":
+        monkeypatch.setenv("NVFP4_DUAL_KERNEL", "single")
+    elif kernel != "auto":
         monkeypatch.setenv("NVFP4_DUAL_KERNEL", "pair")
-    if kernel == "pair96":
-        monkeypatch.setenv("NVFP4_DUAL_BN", "96")
+        monkeypatch.setenv("NVFP4_DUAL_BN", kernel[4:])
     data = I.generate_dual_input(m, n, k, l, seed=1111, device="cuda")
     assert_close(run_dual(data), oracle_dual(data), f"dual {kernel} {m}x{n}x{k}")
-
-
-@pytest.mark.parametrize("m,n,k,l", [(256, 128, 256, 1), (384, 640, 1024, 2), (200, 264, 512, 1),
-                                     (130, 72, 768, 1), (1, 8, 256, 1), (1000, 1000, 2048, 1),
-                                     (128, 1024, 2048, 1), (100, 256, 1024, 3)])
-@pytest.mark.parametrize("bn", ["128", "96"])
-def test_dual_pair_kernel_edges(m, n, k, l, bn, monkeypatch):
-    """CTA-pair kernel (128- and 96-wide tiles): M not a multiple of 256
-    (second CTA partly or wholly past M), N not a multiple of the tile width,
-    batched L."""
-    monkeypatch.setenv("NVFP4_DUAL_KERNEL", "pair")
-    monkeypatch.setenv("NVFP4_DUAL_BN", bn)
-    kernel = f"pair{bn}"
-    data = I.generate_dual_input(m, n, k, l, seed=7 + m + n, device="cuda")
-    assert_close(run_dual(data), oracle_dual(data), f"dual {kernel} {m}x{n}x{k}x{l}")
 
 
 @pytest.mark.parametrize("bn", ["64", "128"])
 @pytest.mark.parametrize("m,n,k,l", DUAL_TASK_TESTS + DUAL_TASK_BENCH + [
     (256, 128, 256, 1), (384, 640, 1024, 2), (200, 264, 512, 1), (130, 72, 768, 1), (1, 8, 256, 1),
-    (1000, 1000, 2048, 1), (100, 256, 1024, 3), (256, 4160, 2048, 1)])
-def test_dual_pair_scale_copy_mode(m, n, k, l, bn, monkeypatch):
-    """CTA-pair kernel in scale-copy mode (each CTA loads half of the tile's
-    B1 and B2 rows, the MMA thread copies the scale atoms into TMEM): task
-    shapes, M and N ragged against the 256-row pair blocks and the tile width
-    (the second CTA's B rows wholly past N at N = 8), batched L, and 64-wide
-    tiles in the upper half of a 128-row scale block."""
-    monkeypatch.setenv("NVFP4_DUAL_KERNEL", "paircp")
+    (1000, 1000, 2048, 1), (100, 256, 1024, 3), (256, 4160, 2048, 1), (128, 1024, 2048, 1)])
+def test_dual_pair_kernel_shapes(m, n, k, l, bn, monkeypatch):
+    """CTA-pair kernel (each CTA loads half of the tile's B1 and B2 rows, the
+    MMA thread copies the scale atoms into TMEM): task shapes, M and N ragged
+    against the 256-row pair blocks and the tile width (the second CTA's B
+    rows wholly past N at N = 8), batched L, and 64-wide tiles in the upper
+    half of a 128-row scale block."""
+    monkeypatch.setenv("NVFP4_DUAL_KERNEL", "pair")
     monkeypatch.setenv("NVFP4_DUAL_BN", bn)
     data = I.generate_dual_input(m, n, k, l, seed=5 + m + n + k, device="cuda")
-    assert_close(run_dual(data), oracle_dual(data), f"dual paircp{bn} {m}x{n}x{k}x{l}")
-
-
-@pytest.mark.parametrize("m,n,k", [(512, 960, 1024), (300, 200, 2048), (256, 96, 256), (768, 2304, 512)])
-def test_dual_pair96_tile_edges(m, n, k, monkeypatch):
-    """CTA-pair kernel with 96-column tiles: scale rows gathered across two
-    128-row atoms, the last tile partly past N, several tiles per pair."""
-    monkeypatch.setenv("NVFP4_DUAL_KERNEL", "pair")
-    monkeypatch.setenv("NVFP4_DUAL_BN", "96")
-    data = I.generate_dual_input(m, n, k, 1, seed=11 + m + n, device="cuda")
-    assert_close(run_dual(data), oracle_dual(data), f"dual pair96 {m}x{n}x{k}")
+    assert_close(run_dual(data), oracle_dual(data), f"dual pair{bn} {m}x{n}x{k}x{l}")
 
 
 @pytest.mark.parametrize("bn", ["64", "128"])
@@ -134,8 +110,9 @@ def test_dual_both_tile_widths(m, n, k, l, bn, monkeypatch):
 
 @pytest.mark.parametrize("m,n,k,l", DUAL_TASK_BENCH)
 def test_dual_benchmark_shapes_automatic_choice(m, n, k, l):
-    """The timed benchmark shapes with no knob set: the automatic kernel and
-    split choice (CTA pair for the 256-row shapes, unsplit otherwise)."""
+    """The timed benchmark shapes with no knob set: the automatic kernel
+    choice (the CTA pair: 64-wide tiles for the 256-row shapes, 128-wide for
+    the 512-row ones)."""
     data = I.generate_dual_input(m, n, k, l, seed=2024 + m, device="cuda")
     assert_close(run_dual(data), oracle_dual(data), f"dual automatic {m}x{n}x{k}")
 

@@ -23,7 +23,7 @@ nvfp4_group_gemm/eval.py:124-128):
   mismatch.  Each case prints its largest absolute and relative error.
 
 No env knobs are set: the kernel and split choices are the automatic ones
-(for the dual benchmark shapes with 128 < M <= 256, the CTA-pair kernel).
+(for the dual benchmark shapes, the CTA-pair kernel).
 """
 import pytest
 import torch

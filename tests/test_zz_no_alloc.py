@@ -11,10 +11,11 @@ inside the library instead of a workspace grown with cudaMalloc.
 These tests call it through the C ABI, twice in a row per shape (the array is
 shared by every call and keeps the previous call's contents), and check each
 result against the CPU oracle within the tolerance the parity tests use, and
-bit for bit against the ordinary entry point.  The shapes cover each branch of
-the kernel choice: a K split through the fixed array, an unsplit call, a
-cluster K split (partials exchanged between CTAs, no array) and the CTA-pair
-kernel.  This file is named to be collected last.
+bit for bit against the ordinary entry point.  The cases cover each branch of
+the kernel choice: the CTA-pair kernel and the single-CTA kernel's cluster K
+split (partials exchanged between CTAs, no array) under the automatic choice,
+and, with the single-CTA kernel forced, its K split through the fixed array
+and its unsplit path.  This file is named to be collected last.
 """
 import numpy as np
 import pytest
@@ -28,13 +29,16 @@ from oracle import nvfp4_oracle as O
 pytestmark = pytest.mark.gpu
 RTOL = ATOL = 1e-2
 
-# (m, n, k, l, branch) -- the branch nvfp4_dual_gemm takes on a 148-SM B200
+# (m, n, k, l, kernel knob, branch) -- the branch nvfp4_dual_gemm takes on a
+# 148-SM B200 (knob None: the automatic choice)
 SHAPES = [
-    (128, 2048, 4096, 1, "K split into 8 through the fixed array"),
-    (128, 1024, 4608, 1, "K split into 9 through the fixed array"),
-    (512, 4096, 1024, 1, "unsplit"),
-    (256, 1024, 8192, 1, "cluster K split (4 CTAs)"),
-    (256, 3072, 4096, 1, "CTA pair"),
+    (128, 2048, 4096, 1, "single", "K split into 8 through the fixed array"),
+    (128, 1024, 4608, 1, "single", "K split into 9 through the fixed array"),
+    (512, 4096, 1024, 1, "single", "unsplit"),
+    (256, 1024, 8192, 1, "single", "cluster K split (4 CTAs)"),
+    (128, 5120, 12288, 1, None, "cluster K split (2 CTAs), automatic"),
+    (256, 3072, 4096, 1, None, "CTA pair, 64-wide tiles"),
+    (512, 3072, 2048, 1, None, "CTA pair, 128-wide tiles"),
 ]
 
 
@@ -55,8 +59,10 @@ def lib(cuda_device):
     return _lib.load()
 
 
-@pytest.mark.parametrize("m,n,k,l,branch", SHAPES, ids=[s[4] for s in SHAPES])
-def test_noalloc_matches_oracle_two_calls(lib, m, n, k, l, branch):
+@pytest.mark.parametrize("m,n,k,l,knob,branch", SHAPES, ids=[s[5] for s in SHAPES])
+def test_noalloc_matches_oracle_two_calls(lib, m, n, k, l, knob, branch, monkeypatch):
+    if knob:
+        monkeypatch.setenv("NVFP4_DUAL_KERNEL", knob)
     d = I.generate_dual_input(m, n, k, l, seed=900 + m + n, device="cuda")
     want = _oracle(d)
     outs = []
