@@ -18,6 +18,7 @@
 #include "dual_gemm.cuh"
 #include "dual_gemm_2sm.cuh"
 #include "grouped_gemm.cuh"
+#include "grouped_gemm_2sm.cuh"
 #include "quantize.cuh"
 #include "moe.cuh"
 
@@ -104,10 +105,11 @@ long long wait_limit_cycles() {
 struct Knobs {
   int dual_group_m = 32;   // NVFP4_DUAL_GROUP_M (measured: 16 -> 32 saves ~1.5% on 8192x14336x4096)
   int dual_splits = 0;     // NVFP4_DUAL_SPLITS (0 = automatic)
-  int dual_bn = 0;         // NVFP4_DUAL_BN (64 / 128, or 64 / 96 / 128 for the pair kernel; 0 = automatic)
+  int dual_bn = 0;         // NVFP4_DUAL_BN (64 / 128; 0 = automatic)
   int dual_kernel = 0;     // NVFP4_DUAL_KERNEL: 0 automatic, 1 pair (CTA-pair kernel), 2 single
   int dual_cluster = 0;    // NVFP4_DUAL_CLUSTER: 0 automatic, 1 off, 2 / 4 forced cluster split-K
   int grouped_bn = 0;      // NVFP4_GROUPED_BN (128 / 256; 0 = automatic)
+  int grouped_kernel = 0;  // NVFP4_GROUPED_KERNEL: 0 automatic, 1 pair (CTA-pair kernel), 2 single
   bool pdl = true;         // NVFP4_PDL=0: launch the GEMMs without programmatic dependent launch
 };
 
@@ -129,6 +131,8 @@ Knobs read_knobs() {
       k.dual_kernel = strcmp(x, "pair") == 0 ? 1 : strcmp(x, "single") == 0 ? 2 : 0;
     else if ((x = val("DUAL_CLUSTER"))) k.dual_cluster = atoi(x);
     else if ((x = val("GROUPED_BN"))) k.grouped_bn = atoi(x);
+    else if ((x = val("GROUPED_KERNEL")))
+      k.grouped_kernel = strcmp(x, "pair") == 0 ? 1 : strcmp(x, "single") == 0 ? 2 : 0;
     else if ((x = val("PDL"))) k.pdl = atoi(x) != 0;
   }
   if (k.dual_group_m < 1) k.dual_group_m = 1;
@@ -611,6 +615,46 @@ int launch_grouped(DeviceState* d, const nvfp4_group* gs, const int* idx, int co
   return launch_grouped_chunk<128, 6, 4, 2, kMaxGroups>(d, base + 1, gs, idx, count, stream);
 }
 
+// CTA-pair grouped kernel: 256x256 tiles, one M=256 x N=256 pair MMA per
+// 64-deep K step, scale atoms copied into TMEM by the MMA thread; four tensor
+// maps per group in the parameter block.
+constexpr int kPairMaxGroups = 48;   // 48 x 4 maps + the table: ~27 KB of parameters
+int launch_grouped_pair(DeviceState* d, const nvfp4_group* gs, const int* idx, int count,
+                        cudaStream_t stream) {
+  using Cfg = GroupedPairCfg<5>;
+  using P = GroupedPairParams<kPairMaxGroups>;
+  auto kern = grouped_gemm_2sm_kernel<5, kPairMaxGroups>;
+  int rc = set_smem_once(d, 16, kern, Cfg::kSmemBytes);
+  if (rc) return rc;
+  static thread_local P p;
+  int tiles = 0;
+  for (int i = 0; i < count; ++i) {
+    const nvfp4_group& g = gs[idx[i]];
+    GroupPairInfo& gi = p.g[i];
+    gi.c = static_cast<__half*>(g.c);
+    gi.m = g.m, gi.n = g.n, gi.k = g.k, gi.l = g.l;
+    gi.mp_blocks = (g.m + 2 * kBM - 1) / (2 * kBM);
+    gi.n_blocks = (g.n + Cfg::kBN - 1) / Cfg::kBN;
+    gi.sfa_blocks = (g.m + 127) / 128;
+    gi.sfb_blocks = (g.n + 127) / 128;
+    gi.tile_start = tiles;
+    gi.lines32 = (g.n % 16 == 0) && (reinterpret_cast<uintptr_t>(g.c) % 32 == 0);
+    tiles += g.l * gi.mp_blocks * gi.n_blocks;
+    const int rest_k = g.k / kKStep;
+    if ((rc = encode_operand(&p.tmap_a[i], g.a, g.m, g.k, g.l, kBM))) return rc;
+    if ((rc = encode_operand(&p.tmap_b[i], g.b, g.n, g.k, g.l, Cfg::kBN / 2))) return rc;
+    if ((rc = encode_sf_atoms(&p.tmap_sfa[i], g.sfa_perm, g.l * gi.sfa_blocks * rest_k))) return rc;
+    if ((rc = encode_sf_atoms(&p.tmap_sfb[i], g.sfb_perm, g.l * gi.sfb_blocks * rest_k))) return rc;
+  }
+  p.num_groups = count;
+  p.tiles = tiles;
+  p.status = d->status;
+  p.wait_limit = wait_limit_cycles();
+  const int pairs = tiles < d->num_sms / 2 ? tiles : d->num_sms / 2;
+  return launch_gemm(kern, (unsigned)(2 * pairs), Cfg::kThreads, Cfg::kSmemBytes, stream, p, 0,
+                     "grouped_gemm_2sm_kernel");
+}
+
 // MoE mode: up to kMoeMaxExpertsPerLaunch experts per launch, sizes read on
 // the device; the grid is persistent over the upper bound of the tiles.
 constexpr int kMoeMaxExpertsPerLaunch = 128;
@@ -795,6 +839,37 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
   t_pdl = kn.pdl;
   const int forced = kn.grouped_bn;
   if (forced == 128 || forced == 256) bn = forced;
+  // The CTA-pair kernel (256x256 tiles) when every group has at least 24 K
+  // blocks and 256 columns, and covering the groups in 256-row pair blocks
+  // costs at most 1.5x the 128-row blocks' rows; it keeps one accumulator,
+  // so with few K blocks per tile its exposed epilogue loses.  Measured on
+  // one B200 (us per call, pair / single-CTA): configuration 3 88.9 / 95.4,
+  // configuration 4 241.8 / 255.0, 8 groups of 64-248 rows x 4096 x 7168
+  // 32.0 / 37.5 (padding 1.45x); with fewer K blocks 8 groups x 7168 x 2048
+  // 26.1 / 22.3, [192, 320] x 3072 x 4096 11.6 / 10.3, [128, 384] x 4096 x
+  // 1536 10.0 / 6.8.
+  bool pair = kn.grouped_kernel == 1;
+  if (kn.grouped_kernel == 0 && forced == 0) {
+    long long rows128 = 0, rows256 = 0;
+    bool long_k = min_n >= 256;
+    for (int i : live) {
+      const nvfp4_group& g = groups[i];
+      long_k = long_k && g.k >= 24 * kBK;
+      rows128 += (long long)g.l * ((g.m + 127) / 128) * 128 * g.n;
+      rows256 += (long long)g.l * ((g.m + 255) / 256) * 256 * g.n;
+    }
+    pair = long_k && 2 * rows256 <= 3 * rows128;
+  }
+  if (pair) {
+    // near-equal chunks of at most kPairMaxGroups groups
+    const int chunks = (n + kPairMaxGroups - 1) / kPairMaxGroups;
+    for (int c = 0, s = 0; c < chunks; ++c) {
+      const int cnt = (n - s) / (chunks - c);
+      if ((rc = launch_grouped_pair(d, groups, live.data() + s, cnt, stream))) return rc;
+      s += cnt;
+    }
+    return NVFP4_OK;
+  }
   if (n <= 16) return launch_grouped<16>(d, groups, live.data(), n, bn, stream);
   for (int s = 0; s < n; s += 96) {
     const int cnt = n - s < 96 ? n - s : 96;

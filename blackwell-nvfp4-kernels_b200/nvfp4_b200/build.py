@@ -17,7 +17,7 @@ CSRC = PKG_DIR.parent / "csrc"
 INCLUDE = PKG_DIR.parent.parent / "include"
 LIB_PATH = PKG_DIR / "libnvfp4_b200.so"
 SOURCES = ["capi.cu"]
-HEADERS = ["ptx.cuh", "kernel_common.cuh", "dual_gemm.cuh", "dual_gemm_2sm.cuh",
+HEADERS = ["ptx.cuh", "kernel_common.cuh", "dual_gemm.cuh", "dual_gemm_2sm.cuh", "grouped_gemm_2sm.cuh",
            "grouped_gemm.cuh", "quantize.cuh", "moe.cuh"]
 
 NVCC_FLAGS = [

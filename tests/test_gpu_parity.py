@@ -249,6 +249,55 @@ def test_group_benchmark_shapes(case, bn, monkeypatch):
                      f"benchmark group case {case} g{i}")
 
 
+@pytest.mark.parametrize("case", range(len(GROUP_TASK_TESTS)))
+def test_group_pair_task_shapes(case, monkeypatch):
+    """CTA-pair grouped kernel (256x256 tiles, groups padded to 256-row pair
+    blocks) on the task's test shapes: every group under 256 rows, so each
+    pair's second CTA is partly or wholly past M."""
+    monkeypatch.setenv("NVFP4_GROUPED_KERNEL", "pair")
+    m, n, k = GROUP_TASK_TESTS[case]
+    data = I.generate_group_input(m, n, k, len(m), seed=1111, device="cuda")
+    outs = G.custom_kernel(data)
+    assert _lib.device_status() == 0
+    for i, (got, want) in enumerate(zip(outs, oracle_group(data))):
+        assert_close(got.cpu().numpy(), want, f"group pair case {case} g{i}")
+
+
+def test_group_pair_ragged_and_chunked(monkeypatch):
+    """CTA-pair grouped kernel: M around the 128/256-row block edges, N below
+    one tile and not a multiple of 256 (second 128-row B block past N, or a
+    single block), K of 1..8 blocks per group, zero-M groups, and more groups
+    than one launch holds (near-equal chunks of at most 48)."""
+    monkeypatch.setenv("NVFP4_GROUPED_KERNEL", "pair")
+    gen = torch.Generator().manual_seed(41)
+    shapes = [(1, 8, 256), (0, 256, 512), (127, 136, 512), (128, 256, 256), (129, 264, 1024),
+              (255, 384, 768), (256, 520, 256), (257, 256, 2048), (640, 1032, 512)]
+    shapes += [(8 * (i % 40 + 1), 256 + 8 * (i % 5), 256 * (i % 3 + 1)) for i in range(50)]
+    pairs = [(torch.randn(m, k, generator=gen), torch.randn(n, k, generator=gen)) for m, n, k in shapes]
+    data = I.group_from_fp32(pairs, device="cuda")
+    outs = G.custom_kernel(data)
+    assert _lib.device_status() == 0
+    for i, (got, want) in enumerate(zip(outs, oracle_group(data))):
+        assert_close(got.cpu().numpy(), want, f"group pair g{i} {shapes[i]}")
+
+
+@pytest.mark.parametrize("kernel", ["pair", "single"])
+def test_group_config3_both_kernels(kernel, monkeypatch):
+    """Configuration 3 under each grouped kernel: sampled rows of every group."""
+    monkeypatch.setenv("NVFP4_GROUPED_KERNEL", kernel)
+    data = I.group_config_input(3, device="cuda")
+    outs = G.custom_kernel(data)
+    assert _lib.device_status() == 0
+    abc, sfab, _, sizes = data
+    for i in range(len(sizes)):
+        (a, b, _), (sa, sb) = abc[i], sfab[i]
+        rows = torch.arange(i % 5, sizes[i][0], 61)
+        want = O.ref_group(_np(_rows(a, rows))[:, :, 0], _np(b)[:, :, 0],
+                           _np(_rows(sa, rows))[:, :, 0], _np(sb)[:, :, 0])
+        assert_close(outs[i][rows.to(outs[i].device), :, 0].cpu().numpy(), want,
+                     f"cfg3 {kernel} group {i} sampled")
+
+
 def test_group_ragged_k_and_chunks():
     # groups of different K (tiles of 2..12 K blocks), ragged M and N, zero-M
     # groups, and more groups than one launch holds
