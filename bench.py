@@ -750,7 +750,9 @@ def run_config(cfg, args, rank, world, device, pg, flush, *, dual_scaling="stron
             pg.barrier()
         torch.cuda.synchronize()
         torch.cuda.nvtx.range_push("timed")
+        launches0 = _lib.load().nvfp4_launch_count()
         per_call_ms = timed_calls(cfg, data, args.steps, flush, stream)
+        launches = _lib.load().nvfp4_launch_count() - launches0
         torch.cuda.nvtx.range_pop()
     if pg:
         pg.barrier()
@@ -825,8 +827,7 @@ def run_config(cfg, args, rank, world, device, pg, flush, *, dual_scaling="stron
     if world > 1:
         roof["note"] = "per rank (rank 0's launches)"
     result["roofline"] = roof
-    launches = 4 if cfg == 6 else 6 if cfg == 7 else len(data) if quant else 1
-    result["gpu_launches"] = args.steps * launches
+    result["gpu_launches"] = launches   # this library's launches in the timed region (its counter)
     result["clocks"] = clocks
 
     if cpu_baseline and rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <atomic>
 #include <mutex>
 #include <unistd.h>
 #include <unordered_map>
@@ -265,9 +266,13 @@ int encode_sf_atoms(CUtensorMap* map, const void* base, int atoms) {
   return cached_map(map, key, [&] { return encode_sf_atoms_uncached(map, base, atoms); });
 }
 
+std::atomic<unsigned long long> g_launches{0};
+
+// Every kernel launch of the library ends here (and is counted).
 int check_launch(const char* what) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "%s launch: %s", what, cudaGetErrorString(e));
+  g_launches.fetch_add(1, std::memory_order_relaxed);
   return NVFP4_OK;
 }
 
@@ -923,6 +928,10 @@ extern "C" const char* nvfp4_status_string(int s) {
 extern "C" const char* nvfp4_last_error(void) { return t_last_error; }
 
 extern "C" int nvfp4_version(void) { return 100; }
+
+extern "C" unsigned long long nvfp4_launch_count(void) {
+  return nvfp4::g_launches.load(std::memory_order_relaxed);
+}
 
 extern "C" int nvfp4_quantize(const float* x, int rows, int k, int l, void* packed,
                               void* sf_perm, void* sf_plain, void* stream_) {

@@ -35,6 +35,7 @@ EXPORTED = (
     "nvfp4_status_string",
     "nvfp4_last_error",
     "nvfp4_version",
+    "nvfp4_launch_count",
 )
 
 
@@ -105,6 +106,8 @@ def load(path: Path | str | None = None) -> ctypes.CDLL:
     lib.nvfp4_last_error.restype = ctypes.c_char_p
     lib.nvfp4_version.argtypes = []
     lib.nvfp4_version.restype = i32
+    lib.nvfp4_launch_count.argtypes = []
+    lib.nvfp4_launch_count.restype = ctypes.c_ulonglong
     if path is None:
         _lib = lib
     return lib

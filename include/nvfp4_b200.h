@@ -163,6 +163,11 @@ const char* nvfp4_last_error(void);
 /* Library version: major*10000 + minor*100 + patch. */
 int nvfp4_version(void);
 
+/* Kernels this library has launched in this process so far (every entry
+ * point, all devices).  Callers read it before and after a region to count
+ * the region's launches.  No reference counterpart. */
+unsigned long long nvfp4_launch_count(void);
+
 #ifdef __cplusplus
 }
 #endif

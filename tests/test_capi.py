@@ -26,7 +26,8 @@ def lib():
 
 def header_functions():
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\**\s+\**(nvfp4_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(
+        r"^\s*(?:const\s+)?(?:(?:unsigned|signed|long|short)\s+)*\w+\**\s+\**(nvfp4_\w+)\s*\(", text, re.M)))
 
 
 def test_header_declares_what_python_binds():
@@ -40,6 +41,7 @@ def test_library_exports_every_header_symbol(lib):
 
 def test_version_and_status_strings(lib):
     assert lib.nvfp4_version() >= 100
+    assert isinstance(lib.nvfp4_launch_count(), int)
     assert lib.nvfp4_status_string(0) == b"ok"
     assert lib.nvfp4_status_string(_lib.NVFP4_ERR_TIMEOUT) == b"device wait timed out"
     assert lib.nvfp4_status_string(-99) == b"unknown status"
