@@ -745,9 +745,14 @@ int run_dual(DeviceState* d, const void* a, const void* b1, const void* b2, cons
   //     256x4096x7168 14.3 / 16.1 / 18.7, 256x3072x4096 10.2 / 11.6 / 12.3,
   //     256x2048x7168 12.2 / 15.1 / 17.1, 256x4096x14336 22.8 / 25.5 / 25.5,
   //     128x4096x7168 15.3 / 15.9 / 18.7, 256x512x1024 6.1 / 7.2 / 6.8;
-  //   otherwise the single-CTA kernel when it would split K (few tiles, at
-  //     least 48 K blocks) and the 128-wide pair tiles leave SMs idle:
-  //     128x7168x16384 (configuration 2) 38.3 pair 128-wide / 36.8 single;
+  //   but with M <= 128 (one 128-row block: the pair's second CTA has no
+  //     rows) and at least 48 K blocks the single-CTA kernel's cluster K
+  //     split: 128x3584x16384 26.2 / 27.7 / 24.4, 128x1792x16384 20.6 / 26.4
+  //     / 19.5, 128x896x16384 19.9 / 25.6 / 17.9 (with 28 K blocks the pair
+  //     still wins: 128x2048x7168 12.2 / 15.0 / 15.1);
+  //   otherwise the single-CTA kernel too when it would split K (at least 48
+  //     K blocks) and the 128-wide pair tiles leave SMs idle:
+  //     128x7168x16384 (configuration 2) 46.3 / 33.3 / 32.3;
   //   otherwise pair 128-wide tiles: 512x4096x7168 21.8 / 16.9 / 18.9,
   //     512x7168x2048 17.0 / 14.1 / 15.2, 1024x4096x7168 36.8 / 27.2 / 33.0,
   //     2048x4096x7168 62.4 / 48.6 / 60.2, 256x7168x2048 11.7 / 10.1 / 11.3,
@@ -761,8 +766,9 @@ int run_dual(DeviceState* d, const void* a, const void* b1, const void* b2, cons
   bool pair = kn.dual_kernel == 1;
   int pair_bn = kn.dual_bn == 64 || kn.dual_bn == 128 ? kn.dual_bn : 0;
   if (!pair && !forced_single && kn.dual_bn == 0) {
-    if (ctas64 <= d->num_sms) pair = true, pair_bn = 64;
-    else if (!(p.k_blocks >= 48 && ctas128 < d->num_sms)) pair = true, pair_bn = 128;
+    const bool long_k = p.k_blocks >= 48, half_idle = m <= kBM;
+    if (ctas64 <= d->num_sms && !(half_idle && long_k)) pair = true, pair_bn = 64;
+    else if (!(long_k && (half_idle || ctas128 < d->num_sms))) pair = true, pair_bn = 128;
   }
   if (pair) {
     if (pair_bn == 0) pair_bn = ctas64 <= d->num_sms ? 64 : 128;
