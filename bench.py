@@ -582,7 +582,7 @@ def load_traffic(workload: str):
         d = json.loads(p.read_text())
         v = d.get(workload)
         if v is not None:
-            return float(v["dram_bytes_per_launch"])
+            return float(v["dram_bytes_per_call"])
     return None
 
 
