@@ -22,7 +22,9 @@
 // * scale factors reach TMEM as in the dual kernel: they land on their own
 //   mbarrier and four staging warps (one per TMEM lane quadrant) write each
 //   stage's atoms with tcgen05.st into that stage's TMEM scale buffer, so
-//   the tensor pipe runs MMAs only (a tcgen05.cp costs it ~50 cycles).
+//   the tensor pipe runs MMAs only.
+// The host picks this kernel for short-K groups and the MoE path; long-K
+// groups go to the CTA-pair kernel (grouped_gemm_2sm.cuh).
 #pragma once
 #include <cuda.h>
 #include "kernel_common.cuh"
