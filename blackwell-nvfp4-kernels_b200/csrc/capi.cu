@@ -638,6 +638,8 @@ int launch_grouped_pair(DeviceState* d, const nvfp4_group* gs, const int* idx, i
     GroupPairInfo& gi = p.g[i];
     gi.c = static_cast<__half*>(g.c);
     gi.m = g.m, gi.n = g.n, gi.k = g.k, gi.l = g.l;
+    const int rem = g.m % (2 * kBM);
+    gi.half = rem != 0 && rem <= kBM;   // the last pair block runs as a half tile
     gi.mp_blocks = (g.m + 2 * kBM - 1) / (2 * kBM);
     gi.n_blocks = (g.n + Cfg::kBN - 1) / Cfg::kBN;
     gi.sfa_blocks = (g.m + 127) / 128;
@@ -646,7 +648,7 @@ int launch_grouped_pair(DeviceState* d, const nvfp4_group* gs, const int* idx, i
     gi.lines32 = (g.n % 16 == 0) && (reinterpret_cast<uintptr_t>(g.c) % 32 == 0);
     tiles += g.l * gi.mp_blocks * gi.n_blocks;
     const int rest_k = g.k / kKStep;
-    if ((rc = encode_operand(&p.tmap_a[i], g.a, g.m, g.k, g.l, kBM))) return rc;
+    if ((rc = encode_operand(&p.tmap_a[i], g.a, g.m, g.k, g.l, kBM / 2))) return rc;
     if ((rc = encode_operand(&p.tmap_b[i], g.b, g.n, g.k, g.l, Cfg::kBN / 2))) return rc;
     if ((rc = encode_sf_atoms(&p.tmap_sfa[i], g.sfa_perm, g.l * gi.sfa_blocks * rest_k))) return rc;
     if ((rc = encode_sf_atoms(&p.tmap_sfb[i], g.sfb_perm, g.l * gi.sfb_blocks * rest_k))) return rc;

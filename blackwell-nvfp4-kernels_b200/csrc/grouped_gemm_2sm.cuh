@@ -21,9 +21,15 @@
 //   travels in the kernel parameter block; tiles are listed group-major with
 //   pair M-blocks fastest inside a column, and every pair walks the list
 //   round-robin, finding its group by binary search over the tile starts;
-// * a group's rows are covered in 256-row pair blocks: rows past M_g load as
-//   TMA zero fill and are not stored (the host uses this kernel only where
-//   that padding costs little);
+// * a group's rows are covered in 256-row pair blocks, except that a last
+//   block holding at most 128 rows is a "half tile": the pair computes its
+//   128 x 256 block of C transposed, Cᵀ = B . Aᵀ, with the tile's B rows as
+//   the M = 256 operand (128 per CTA) and the block's A rows as the N = 128
+//   operand (64 per CTA), so no CTA works on rows past M (per SM and K
+//   block: 8 + 16 KB of operands for 128 x 128 outputs).  Half tiles keep
+//   their place in the list, next to the group's other blocks of the same
+//   columns, which read the same B rows from L2; rows past M_g in a full
+//   tile's second CTA load as TMA zero fill and are not stored;
 // * issue threads chosen with elect.sync, descriptors advanced from the
 //   stage-0 ones, one accumulator that the eight epilogue warps of each CTA
 //   pull into registers and release before the stores, all waits bounded.
@@ -37,13 +43,14 @@ struct GroupPairInfo {
   __half* c;              // [L][M][N]
   int m, n, k, l;
   int mp_blocks, n_blocks, tile_start;   // 256-row pair blocks, 256-column blocks
+  int half;                              // the last pair block holds <= 128 rows
   int sfa_blocks, sfb_blocks;            // ceil(M/128), ceil(N/128)
   int lines32;                           // C rows start 32-byte aligned
 };
 
 template <int kMaxGroups>
 struct GroupedPairParams {
-  CUtensorMap tmap_a[kMaxGroups];    // bytes [L][M][K/2], box {128 B, 128 rows, 1}
+  CUtensorMap tmap_a[kMaxGroups];    // bytes [L][M][K/2], box {128 B, 64 rows, 1}
   CUtensorMap tmap_b[kMaxGroups];    // bytes [L][N][K/2], box {128 B, 128 rows, 1}
   // scale atoms [L * blocks * K/64][128 x 32-bit], box {128, 4}: the four
   // atoms of one 256-deep K block of one 128-row block
@@ -65,6 +72,9 @@ struct GroupedPairCfg {
   static constexpr int kSfbBytes = 2 * kSfStageBytes;  // 4 atoms of each of the tile's B blocks
   static constexpr int kStageBytes = kABytes + kBBytes + kSfaBytes + kSfbBytes;   // 38 KB
   static constexpr int kPairTxBytes = 2 * kStageBytes;  // both CTAs' copies of a stage
+  // half tile, per CTA: 64 A rows, 128 B rows, the atoms of its B block and of the A block
+  static constexpr int kHalfABytes = kABytes / 2;
+  static constexpr int kHalfPairTxBytes = 2 * (kHalfABytes + kBBytes + 2 * kSfStageBytes);
   static constexpr int kEpiWarps = 8;                   // 2 per TMEM quadrant
   static constexpr int kColsPerWarp = kBN / 2;         // 128
   // warp roles: epilogue [0, 8), tile producer 8, MMA 9, scale producer 10
@@ -79,7 +89,7 @@ struct GroupedPairCfg {
   static_assert(kSfCol + kStages * kSfBufCols <= kTmemCols, "TMEM budget: one scale buffer per stage");
 };
 
-struct GPairTile { int g, l, mp, nb; };
+struct GPairTile { int g, l, mp, nb; bool half; };
 
 template <int kMaxGroups>
 __device__ __forceinline__ GPairTile gpair_tile(const GroupedPairParams<kMaxGroups>& p, int t) {
@@ -97,6 +107,7 @@ __device__ __forceinline__ GPairTile gpair_tile(const GroupedPairParams<kMaxGrou
   local -= r.l * per_l;
   r.mp = local % gi.mp_blocks;
   r.nb = local / gi.mp_blocks;
+  r.half = gi.half && r.mp == gi.mp_blocks - 1;
   return r;
 }
 
@@ -170,17 +181,20 @@ grouped_gemm_2sm_kernel(const __grid_constant__ GroupedPairParams<kMaxGroups> p)
         }
         const int k_blocks = gi.k / kBK;
         const int rest_k = gi.k / kKStep;   // 64-deep atoms per 128-row block
-        const int m0 = tc.mp * 2 * kBM + (int)rank * kBM;            // this CTA's A rows
         const int nb0 = tc.nb * Cfg::kBN + (int)rank * (Cfg::kBN / 2);   // this CTA's B rows
-        // a CTA wholly past M re-reads the last real A scale block (its rows
-        // load as zeros and are never stored); a second B block past N
-        // likewise re-reads the last real one
-        const int ablk = min(m0 / 128, gi.sfa_blocks - 1);
-        const int blk0 = tc.nb * (Cfg::kBN / 128);
-        const int blk1 = min(blk0 + 1, gi.sfb_blocks - 1);
+        // full tile: this CTA's 128 A rows, their scale block and the tile's
+        // two B blocks.  Half tile: 64 of the block's A rows (the N = 128
+        // operand), this CTA's own B block (the M = 256 operand's scales)
+        // and the A block.  A B block past N re-reads the last real one
+        // (its columns are never stored).
+        const int m0 = tc.mp * 2 * kBM + (int)rank * (tc.half ? kBM / 2 : kBM);
+        const int ablk = min(tc.mp * 2 + (tc.half ? 0 : (int)rank), gi.sfa_blocks - 1);
+        const int blk0 = min(tc.nb * (Cfg::kBN / 128) + (tc.half ? (int)rank : 0), gi.sfb_blocks - 1);
+        const int blk1 = min(tc.nb * (Cfg::kBN / 128) + 1, gi.sfb_blocks - 1);
         const int a_atom0 = (tc.l * gi.sfa_blocks + ablk) * rest_k;
         const int b_atom0 = (tc.l * gi.sfb_blocks + blk0) * rest_k;
         const int b_atom1 = (tc.l * gi.sfb_blocks + blk1) * rest_k;
+        const uint32_t tx = tc.half ? Cfg::kHalfPairTxBytes : Cfg::kPairTxBytes;
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!ctl.wait(smem_u32(&bar_empty[stage]), phase ^ 1u, kDevTimeoutStageFree)) {
             ok = false;
@@ -190,17 +204,26 @@ grouped_gemm_2sm_kernel(const __grid_constant__ GroupedPairParams<kMaxGroups> p)
           const uint32_t sb = sa + Cfg::kABytes;
           const uint32_t full = mapa_shared(smem_u32(&bar_full[stage]), 0);
           if (tile_role) {
-            if (leader) mbar_arrive_expect_tx(smem_u32(&bar_full[stage]), Cfg::kPairTxBytes);
+            if (leader) mbar_arrive_expect_tx(smem_u32(&bar_full[stage]), tx);
             tma_load_3d_pair(sa, &p.tmap_a[tc.g], full, kb * 128, m0, tc.l, pol);
+            if (!tc.half)
+              tma_load_3d_pair(sa + Cfg::kHalfABytes, &p.tmap_a[tc.g], full, kb * 128, m0 + kBM / 2,
+                               tc.l, pol);
             tma_load_3d_pair(sb, &p.tmap_b[tc.g], full, kb * 128, nb0, tc.l, pol);
           } else {
-            // [SFA][SFB block 0][SFB block 1], 4 atoms each
+            // full tile: [SFA][SFB block 0][SFB block 1]; half tile: [SFB
+            // block of this CTA][SFA], 4 atoms each
             const uint32_t ssf = sb + Cfg::kBBytes;
             const int ka = kb * (kBK / kKStep);
-            tma_load_2d_pair(ssf, &p.tmap_sfa[tc.g], full, 0, a_atom0 + ka, pol);
-            tma_load_2d_pair(ssf + Cfg::kSfaBytes, &p.tmap_sfb[tc.g], full, 0, b_atom0 + ka, pol);
-            tma_load_2d_pair(ssf + Cfg::kSfaBytes + kSfStageBytes, &p.tmap_sfb[tc.g], full, 0,
-                             b_atom1 + ka, pol);
+            if (tc.half) {
+              tma_load_2d_pair(ssf, &p.tmap_sfb[tc.g], full, 0, b_atom0 + ka, pol);
+              tma_load_2d_pair(ssf + kSfStageBytes, &p.tmap_sfa[tc.g], full, 0, a_atom0 + ka, pol);
+            } else {
+              tma_load_2d_pair(ssf, &p.tmap_sfa[tc.g], full, 0, a_atom0 + ka, pol);
+              tma_load_2d_pair(ssf + Cfg::kSfaBytes, &p.tmap_sfb[tc.g], full, 0, b_atom0 + ka, pol);
+              tma_load_2d_pair(ssf + Cfg::kSfaBytes + kSfStageBytes, &p.tmap_sfb[tc.g], full, 0,
+                               b_atom1 + ka, pol);
+            }
           }
           issued |= 1u << stage;
           last_phase = (last_phase & ~(1u << stage)) | (phase << stage);
@@ -218,9 +241,11 @@ grouped_gemm_2sm_kernel(const __grid_constant__ GroupedPairParams<kMaxGroups> p)
   } else if (warp == Cfg::kMmaWarp) {
     // ------------------------------------------------------------ MMA issuer (leader only)
     if (leader && elect_one()) {
-      // M = 256, N = 256, e2m1 x e2m1, e4m3 scales
+      // e2m1 x e2m1, e4m3 scales; M = 256 and N = 256 (full tile) or 128 (half tile)
       constexpr uint32_t idesc = (1u << 7) | (1u << 10) | ((uint32_t)(Cfg::kBN >> 3) << 17) |
                                  ((uint32_t)(256 >> 4) << 24);
+      constexpr uint32_t idesc_half = (1u << 7) | (1u << 10) | ((uint32_t)(128 >> 3) << 17) |
+                                      ((uint32_t)(256 >> 4) << 24);
       constexpr uint16_t kBoth = 0x3;
       const uint64_t a_desc0 = kmajor_sw128_desc(smem_base);   // stage 0's A tile
       const uint64_t sf_desc0 = sf_atom_desc(smem_base + Cfg::kABytes + Cfg::kBBytes);   // its first SFA atom
@@ -228,7 +253,8 @@ grouped_gemm_2sm_kernel(const __grid_constant__ GroupedPairParams<kMaxGroups> p)
       uint32_t phase = 0, acc_phase = 0;
       bool ok = true, any = false;
       for (int t = pair; t < p.tiles && ok; t += num_pairs) {
-        const int k_blocks = p.g[gpair_tile(p, t).g].k / kBK;
+        const GPairTile tc = gpair_tile(p, t);
+        const int k_blocks = p.g[tc.g].k / kBK;
         if (!ctl.wait(smem_u32(&bar_acc_empty), acc_phase ^ 1u, kDevTimeoutAccFree)) {
           ok = false;
           break;
@@ -247,16 +273,30 @@ grouped_gemm_2sm_kernel(const __grid_constant__ GroupedPairParams<kMaxGroups> p)
           const uint64_t dsf = desc_advance(sf_desc0, so);
           const uint32_t sf_a = tmem + Cfg::kSfCol + stage * Cfg::kSfBufCols;
           const uint32_t sf_b = sf_a + 16;
-          // per 64-deep step j: its SFA atom into columns [4j, +4), the two B
-          // blocks' atoms into [16 + 8j, +8) (B rows 0-127, then 128-255), then the MMA
-          #pragma unroll
-          for (int j = 0; j < kBK / kKStep; ++j) {
-            const uint64_t dsa = desc_advance(dsf, j * kSfAtom);
-            tc_cp_pair_32x128b_x4(sf_a + 4 * j, dsa);
-            tc_cp_pair_32x128b_x4(sf_b + 8 * j, desc_advance(dsa, Cfg::kSfaBytes));
-            tc_cp_pair_32x128b_x4(sf_b + 8 * j + 4, desc_advance(dsa, Cfg::kSfaBytes + kSfStageBytes));
-            tc_mma_nvf4_pair(tmem, desc_advance(da, 32 * j), desc_advance(db, 32 * j), idesc,
-                             sf_a + 4 * j, sf_b + 8 * j, (kb | j) != 0);
+          if (tc.half) {
+            // Cᵀ block: the CTA's B rows are the M operand (its B block's
+            // atom into [4j, +4)), the A rows the N operand (the A block's
+            // atom into [16 + 8j, +4))
+            #pragma unroll
+            for (int j = 0; j < kBK / kKStep; ++j) {
+              const uint64_t dsa = desc_advance(dsf, j * kSfAtom);
+              tc_cp_pair_32x128b_x4(sf_a + 4 * j, dsa);
+              tc_cp_pair_32x128b_x4(sf_b + 8 * j, desc_advance(dsa, kSfStageBytes));
+              tc_mma_nvf4_pair(tmem, desc_advance(db, 32 * j), desc_advance(da, 32 * j), idesc_half,
+                               sf_a + 4 * j, sf_b + 8 * j, (kb | j) != 0);
+            }
+          } else {
+            // per 64-deep step j: its SFA atom into columns [4j, +4), the two B
+            // blocks' atoms into [16 + 8j, +8) (B rows 0-127, then 128-255), then the MMA
+            #pragma unroll
+            for (int j = 0; j < kBK / kKStep; ++j) {
+              const uint64_t dsa = desc_advance(dsf, j * kSfAtom);
+              tc_cp_pair_32x128b_x4(sf_a + 4 * j, dsa);
+              tc_cp_pair_32x128b_x4(sf_b + 8 * j, desc_advance(dsa, Cfg::kSfaBytes));
+              tc_cp_pair_32x128b_x4(sf_b + 8 * j + 4, desc_advance(dsa, Cfg::kSfaBytes + kSfStageBytes));
+              tc_mma_nvf4_pair(tmem, desc_advance(da, 32 * j), desc_advance(db, 32 * j), idesc,
+                               sf_a + 4 * j, sf_b + 8 * j, (kb | j) != 0);
+            }
           }
           tc_commit_pair(smem_u32(&bar_empty[stage]), kBoth);   // stage (and scale buffer) free
           any = true;
@@ -283,6 +323,33 @@ grouped_gemm_2sm_kernel(const __grid_constant__ GroupedPairParams<kMaxGroups> p)
       const GroupPairInfo& gi = p.g[tc.g];
       if (!ctl.wait(smem_u32(&bar_acc_full), acc_phase, kDevTimeoutAccFull)) break;
       tc_fence_after();
+      if (tc.half) {
+        // Cᵀ block: TMEM lane = C column nb*256 + 128*rank + lane, TMEM column
+        // j = C row 256*mp + j; the warp pulls columns [64*part, +64), hands
+        // TMEM back, and stores one C row per register (32 lanes = 64
+        // contiguous bytes)
+        const uint32_t t_acc = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(64 * part);
+        uint32_t v[2][32];
+        tmem_ld_32x32b_x32(t_acc, v[0]);
+        tmem_ld_32x32b_x32(t_acc + 32, v[1]);
+        tmem_ld_wait();
+        tmem_regs_ready(v[0]);
+        tmem_regs_ready(v[1]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(acc_empty_leader);
+        acc_phase ^= 1u;
+        const int col = tc.nb * Cfg::kBN + (int)rank * (Cfg::kBN / 2) + quad * 32 + (int)lane;
+        const int row0 = tc.mp * 2 * kBM + 64 * part;
+        if (col < gi.n) {
+          __half* c0 = gi.c + ((size_t)tc.l * gi.m + row0) * (size_t)gi.n + col;
+          const int rows = min(64, gi.m - row0);
+          #pragma unroll
+          for (int e = 0; e < 64; ++e)
+            if (e < rows) c0[(size_t)e * gi.n] = __float2half_rn(__uint_as_float(v[e >> 5][e & 31]));
+        }
+        continue;
+      }
       const uint32_t t_acc = tmem + ((uint32_t)(quad * 32) << 16) + (uint32_t)(kCW * part);
       // pull the warp's 128 columns into registers, hand TMEM back, pack to
       // fp16 (two 64-column lines per lane), then store whole lines

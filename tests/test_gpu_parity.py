@@ -251,9 +251,10 @@ def test_group_benchmark_shapes(case, bn, monkeypatch):
 
 @pytest.mark.parametrize("case", range(len(GROUP_TASK_TESTS)))
 def test_group_pair_task_shapes(case, monkeypatch):
-    """CTA-pair grouped kernel (256x256 tiles, groups padded to 256-row pair
-    blocks) on the task's test shapes: every group under 256 rows, so each
-    pair's second CTA is partly or wholly past M."""
+    """CTA-pair grouped kernel (256x256 tiles; a last block of at most 128
+    rows runs as a transposed 128x256 half tile) on the task's test shapes:
+    every group under 256 rows, so each is one full tile with its second CTA
+    partly past M, or one half tile."""
     monkeypatch.setenv("NVFP4_GROUPED_KERNEL", "pair")
     m, n, k = GROUP_TASK_TESTS[case]
     data = I.generate_group_input(m, n, k, len(m), seed=1111, device="cuda")
@@ -264,10 +265,12 @@ def test_group_pair_task_shapes(case, monkeypatch):
 
 
 def test_group_pair_ragged_and_chunked(monkeypatch):
-    """CTA-pair grouped kernel: M around the 128/256-row block edges, N below
-    one tile and not a multiple of 256 (second 128-row B block past N, or a
-    single block), K of 1..8 blocks per group, zero-M groups, and more groups
-    than one launch holds (near-equal chunks of at most 48)."""
+    """CTA-pair grouped kernel: M around the 128/256-row block edges (half
+    tiles of 1, 64, 127, 128 rows; full tiles whose second CTA holds 1 or 127
+    rows), N below one tile and not a multiple of 256 (second 128-row B block
+    past N, or a single block: a half tile's second CTA then stores nothing),
+    K of 1..8 blocks per group, zero-M groups, and more groups than one launch
+    holds (near-equal chunks of at most 48)."""
     monkeypatch.setenv("NVFP4_GROUPED_KERNEL", "pair")
     gen = torch.Generator().manual_seed(41)
     shapes = [(1, 8, 256), (0, 256, 512), (127, 136, 512), (128, 256, 256), (129, 264, 1024),
