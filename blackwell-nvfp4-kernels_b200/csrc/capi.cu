@@ -625,7 +625,7 @@ int launch_grouped(DeviceState* d, const nvfp4_group* gs, const int* idx, int co
 // maps per group in the parameter block.
 constexpr int kPairMaxGroups = 48;   // 48 x 4 maps + the table: ~27 KB of parameters
 int launch_grouped_pair(DeviceState* d, const nvfp4_group* gs, const int* idx, int count,
-                        cudaStream_t stream) {
+                        bool chained, cudaStream_t stream) {
   using Cfg = GroupedPairCfg<5>;
   using P = GroupedPairParams<kPairMaxGroups>;
   auto kern = grouped_gemm_2sm_kernel<5, kPairMaxGroups>;
@@ -655,6 +655,7 @@ int launch_grouped_pair(DeviceState* d, const nvfp4_group* gs, const int* idx, i
   }
   p.num_groups = count;
   p.tiles = tiles;
+  p.chained = chained;
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
   const int pairs = tiles < d->num_sms / 2 ? tiles : d->num_sms / 2;
@@ -878,7 +879,7 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
     const int chunks = (n + kPairMaxGroups - 1) / kPairMaxGroups;
     for (int c = 0, s = 0; c < chunks; ++c) {
       const int cnt = (n - s) / (chunks - c);
-      if ((rc = launch_grouped_pair(d, groups, live.data() + s, cnt, stream))) return rc;
+      if ((rc = launch_grouped_pair(d, groups, live.data() + s, cnt, s > 0, stream))) return rc;
       s += cnt;
     }
     return NVFP4_OK;

@@ -58,6 +58,10 @@ struct GroupedPairParams {
   CUtensorMap tmap_sfb[kMaxGroups];
   GroupPairInfo g[kMaxGroups];
   int num_groups, tiles;
+  // a later launch of the same call (other groups, same inputs' producers):
+  // it may start on SMs the previous launch frees, and waits for that launch
+  // before it exits instead of before it starts
+  int chained;
   unsigned* status;
   long long wait_limit;
 };
@@ -148,8 +152,10 @@ grouped_gemm_2sm_kernel(const __grid_constant__ GroupedPairParams<kMaxGroups> p)
   cluster_sync();   // the peer's barriers exist before anyone signals them
   tc_fence_after();
   const uint32_t tmem = s_tmem_base;
-  // the prologue above overlaps the previous kernel; global memory only after it
-  griddep_wait();
+  // the prologue above overlaps the previous kernel; global memory only after
+  // it.  A chained launch reads nothing the previous one writes: that launch
+  // let it start only after its own wait, so the inputs are complete.
+  if (!p.chained) griddep_wait();
   if (threadIdx.x == 0) griddep_launch_dependents();
   const AbortCtl ctl{&s_abort, p.status, p.wait_limit};
 
@@ -394,6 +400,9 @@ grouped_gemm_2sm_kernel(const __grid_constant__ GroupedPairParams<kMaxGroups> p)
     tc_fence_after();
     tmem_dealloc_pair<Cfg::kTmemCols>(tmem);
   }
+  // a chained launch completes only after the previous one: whatever waits
+  // for this kernel then sees every launch of the call done
+  if (p.chained && threadIdx.x == 0) griddep_wait();
 }
 
 }  // namespace nvfp4
