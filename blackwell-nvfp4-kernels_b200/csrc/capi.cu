@@ -578,7 +578,7 @@ int launch_dual_2sm(DeviceState* d, int slot, const void* a, const void* b1, con
 // ---------------------------------------------------------------- grouped GEMM
 template <int kBN, int kStages, int kEpiWarps, int kAccBufs, int kMaxGroups>
 int launch_grouped_chunk(DeviceState* d, int slot, const nvfp4_group* gs, const int* idx, int count,
-                         cudaStream_t stream) {
+                         bool chained, cudaStream_t stream) {
   using Cfg = GroupedCfg<kBN, kStages, kEpiWarps, kAccBufs>;
   auto kern = grouped_gemm_kernel<kBN, kStages, kEpiWarps, kAccBufs, GroupedParams<kMaxGroups>>;
   int rc = set_smem_once(d, slot, kern, Cfg::kSmemBytes);
@@ -602,6 +602,7 @@ int launch_grouped_chunk(DeviceState* d, int slot, const nvfp4_group* gs, const 
   }
   p.num_groups = count;
   p.tiles = tiles;
+  p.chained = chained;
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
   const int grid = tiles < d->num_sms ? tiles : d->num_sms;
@@ -614,10 +615,11 @@ int launch_grouped_chunk(DeviceState* d, int slot, const nvfp4_group* gs, const 
 // accumulator buffers).
 template <int kMaxGroups>
 int launch_grouped(DeviceState* d, const nvfp4_group* gs, const int* idx, int count, int bn,
-                   cudaStream_t stream) {
+                   bool chained, cudaStream_t stream) {
   const int base = kMaxGroups == 16 ? 4 : 6;
-  if (bn == 256) return launch_grouped_chunk<256, 4, 8, 1, kMaxGroups>(d, base, gs, idx, count, stream);
-  return launch_grouped_chunk<128, 6, 4, 2, kMaxGroups>(d, base + 1, gs, idx, count, stream);
+  if (bn == 256)
+    return launch_grouped_chunk<256, 4, 8, 1, kMaxGroups>(d, base, gs, idx, count, chained, stream);
+  return launch_grouped_chunk<128, 6, 4, 2, kMaxGroups>(d, base + 1, gs, idx, count, chained, stream);
 }
 
 // CTA-pair grouped kernel: 256x256 tiles, one M=256 x N=256 pair MMA per
@@ -688,6 +690,7 @@ int launch_moe_grouped_chunk(DeviceState* d, int slot, const void* a, int a_rows
   p.c = static_cast<__half*>(c);
   p.e0 = e0, p.experts = count, p.n = n, p.k = k;
   p.lines32 = (n % 16 == 0) && (reinterpret_cast<uintptr_t>(c) % 32 == 0);
+  p.chained = 0;
   p.status = d->status;
   p.wait_limit = wait_limit_cycles();
   // tiles <= (ceil(rows / 128) + experts) * n_blocks whatever the routing
@@ -884,10 +887,11 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
     }
     return NVFP4_OK;
   }
-  if (n <= 16) return launch_grouped<16>(d, groups, live.data(), n, bn, stream);
+  if (n <= 16) return launch_grouped<16>(d, groups, live.data(), n, bn, false, stream);
+  // later chunks chained, as for the pair kernel
   for (int s = 0; s < n; s += 96) {
     const int cnt = n - s < 96 ? n - s : 96;
-    if ((rc = launch_grouped<96>(d, groups, live.data() + s, cnt, bn, stream))) return rc;
+    if ((rc = launch_grouped<96>(d, groups, live.data() + s, cnt, bn, s > 0, stream))) return rc;
   }
   return NVFP4_OK;
 }

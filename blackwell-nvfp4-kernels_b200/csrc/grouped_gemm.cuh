@@ -46,6 +46,7 @@ struct GroupedParams {
   CUtensorMap tmap_b[kMaxGroups];  // bytes [L][N][K/2], box {128 B, BN rows, 1}
   GroupInfo g[kMaxGroups];
   int num_groups, tiles;
+  int chained;   // a later launch of the same call: see the CTA-pair kernel
   unsigned* status;
   long long wait_limit;
 };
@@ -90,6 +91,7 @@ struct MoeGemmParams {
   const int* atom_offsets;
   __half* c;                         // [rows][N]
   int e0, experts, n, k, lines32;
+  int chained;                       // always 0: one launch per dispatch chunk waits as usual
   unsigned* status;
   long long wait_limit;
 };
@@ -237,8 +239,10 @@ grouped_gemm_kernel(const __grid_constant__ P p) {
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = s_tmem_base;
-  // the prologue above overlaps the previous kernel; global memory only after it
-  griddep_wait();
+  // the prologue above overlaps the previous kernel; global memory only after
+  // it (a chained launch reads nothing the previous one writes; it waits for
+  // it before exiting instead)
+  if (!p.chained) griddep_wait();
   if (threadIdx.x == 0) griddep_launch_dependents();
   const AbortCtl ctl{&s_abort, p.status, p.wait_limit};
   Sched sched(p, s_sched);
@@ -487,6 +491,7 @@ grouped_gemm_kernel(const __grid_constant__ P p) {
     tc_fence_after();
     tmem_dealloc<Cfg::kTmemCols>(tmem);
   }
+  if (p.chained && threadIdx.x == 0) griddep_wait();
 }
 
 }  // namespace nvfp4

@@ -284,6 +284,23 @@ def test_group_pair_ragged_and_chunked(monkeypatch):
         assert_close(got.cpu().numpy(), want, f"group pair g{i} {shapes[i]}")
 
 
+def test_group_auto_pair_tails():
+    """Automatic choice with long K (the CTA-pair kernel, no override): last
+    blocks of at most 128 rows as half tiles — whole groups of <= 128 rows
+    and the tails of larger groups (44 and 128 rows after 256, 128 after
+    512, 232 after 768 as a full block) — and a 129-row group as one full
+    pair block whose second CTA holds one row."""
+    gen = torch.Generator().manual_seed(53)
+    shapes = [(300, 256, 6144), (384, 384, 6144), (640, 264, 6144), (1000, 256, 6144),
+              (129, 384, 6144), (100, 256, 6144), (64, 272, 6144)]
+    pairs = [(torch.randn(m, k, generator=gen), torch.randn(n, k, generator=gen)) for m, n, k in shapes]
+    data = I.group_from_fp32(pairs, device="cuda")
+    outs = G.custom_kernel(data)
+    assert _lib.device_status() == 0
+    for i, (got, want) in enumerate(zip(outs, oracle_group(data))):
+        assert_close(got.cpu().numpy(), want, f"group auto split g{i} {shapes[i]}")
+
+
 @pytest.mark.parametrize("kernel", ["pair", "single"])
 def test_group_config3_both_kernels(kernel, monkeypatch):
     """Configuration 3 under each grouped kernel: sampled rows of every group."""
