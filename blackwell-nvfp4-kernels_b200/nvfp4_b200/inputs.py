@@ -93,27 +93,35 @@ def dual_config_input(cfg: int, device="cuda", quantize_on=None):
 
 
 def group_from_fp32(pairs, device="cuda", quantize_on=None):
-    """[(A_g [M,K] fp32, B_g [N,K] fp32)] -> the reference's grouped 4-tuple (L=1)."""
+    """[(A_g, B_g)] fp32, A_g [M,K] and B_g [N,K] (L=1) or A_g [L,M,K] and
+    B_g [L,N,K] (batched) -> the reference's grouped 4-tuple, every tensor in
+    its layout: [rows, K/2, L] K-major with L outermost in memory."""
     quantize_on = quantize_on or device
     dev = torch.device(device)
     abc, sfab, sfab_perm, sizes = [], [], [], []
     for a, b in pairs:
-        m, k = a.shape
-        n = b.shape[0]
+        a3 = a if a.dim() == 3 else a.unsqueeze(0)
+        b3 = b if b.dim() == 3 else b.unsqueeze(0)
+        l, m, k = a3.shape
+        n = b3.shape[1]
         if m > 0:
-            pa, sa = _pack_operand(a, quantize_on)
+            pk = [_pack_operand(a3[i], quantize_on) for i in range(l)]
+            pa = torch.stack([p_[0] for p_ in pk])
+            sa = torch.stack([p_[1] for p_ in pk])
         else:
-            pa = torch.zeros((0, k // 2), dtype=torch.uint8)
-            sa = torch.zeros((0, k // SF_VEC), dtype=torch.uint8)
-        pb, sb = _pack_operand(b, quantize_on)
-        fp4 = lambda t: t.to(dev).unsqueeze(0).permute(1, 2, 0).view(torch.float4_e2m1fn_x2)
-        sf3 = lambda t: t.to(dev).view(torch.float8_e4m3fn).unsqueeze(0).permute(1, 2, 0)
-        c = torch.zeros((1, m, n), dtype=torch.float16, device=dev).permute(1, 2, 0)
+            pa = torch.zeros((l, 0, k // 2), dtype=torch.uint8)
+            sa = torch.zeros((l, 0, k // SF_VEC), dtype=torch.uint8)
+        pk = [_pack_operand(b3[i], quantize_on) for i in range(l)]
+        pb = torch.stack([p_[0] for p_ in pk])
+        sb = torch.stack([p_[1] for p_ in pk])
+        fp4 = lambda t: t.to(dev).permute(1, 2, 0).view(torch.float4_e2m1fn_x2)
+        sf3 = lambda t: t.to(dev).view(torch.float8_e4m3fn).permute(1, 2, 0)
+        c = torch.zeros((l, m, n), dtype=torch.float16, device=dev).permute(1, 2, 0)
         sfa, sfb = sf3(sa), sf3(sb)
         abc.append((fp4(pa), fp4(pb), c))
         sfab.append((sfa, sfb))
         sfab_perm.append((swizzle_sf(sfa), swizzle_sf(sfb)))
-        sizes.append((m, n, k, 1))
+        sizes.append((m, n, k, l))
     return abc, sfab, sfab_perm, sizes
 
 

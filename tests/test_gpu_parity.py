@@ -301,6 +301,26 @@ def test_group_auto_pair_tails():
         assert_close(got.cpu().numpy(), want, f"group auto split g{i} {shapes[i]}")
 
 
+@pytest.mark.parametrize("kernel", ["auto", "pair", "single"])
+def test_group_batched_l(kernel, monkeypatch):
+    """Groups with L = 2 and 3 batches (A, B, scales and C with L outermost
+    in memory, as the reference lays them out): full and half pair tiles,
+    ragged N, a zero-M group, under each grouped kernel."""
+    if kernel != "auto":
+        monkeypatch.setenv("NVFP4_GROUPED_KERNEL", kernel)
+    gen = torch.Generator().manual_seed(67)
+    shapes = [(200, 256, 6144, 2), (300, 384, 6144, 3), (64, 264, 6144, 2), (0, 256, 6144, 2),
+              (384, 256, 6144, 2)]
+    pairs = [(torch.randn(l, m, k, generator=gen), torch.randn(l, n, k, generator=gen))
+             for m, n, k, l in shapes]
+    data = I.group_from_fp32(pairs, device="cuda")
+    outs = G.custom_kernel(data)
+    assert _lib.device_status() == 0
+    for i, (got, want) in enumerate(zip(outs, oracle_group(data))):
+        assert got.shape == want.shape
+        assert_close(got.cpu().numpy(), want, f"group L>1 {kernel} g{i} {shapes[i]}")
+
+
 @pytest.mark.parametrize("kernel", ["pair", "single"])
 def test_group_config3_both_kernels(kernel, monkeypatch):
     """Configuration 3 under each grouped kernel: sampled rows of every group."""
