@@ -844,48 +844,75 @@ def run_config(cfg, args, rank, world, device, pg, flush, *, dual_scaling="stron
     return result
 
 
+def _clone_data(x):
+    """A second set of a GEMM configuration's device tensors (same shapes and
+    strides; one-byte types copied as bytes)."""
+    if isinstance(x, torch.Tensor):
+        if x.element_size() == 1 and x.dtype != torch.uint8:
+            return x.view(torch.uint8).clone().view(x.dtype)
+        return x.clone()
+    if isinstance(x, tuple):
+        return tuple(_clone_data(v) for v in x)
+    if isinstance(x, list):
+        return [_clone_data(v) for v in x]
+    return x
+
+
 def e2e_leg(cfg, data, args, device, stream, pg, flop_all, bytes_all):
     """The metric through the public API with pinned host buffers.  Every step
-    uploads its inputs and reads its result back; the upload of step i+1 runs
-    on its own stream while step i's result is read back on another (PCIe is
-    full duplex), and a step's compute waits for its inputs and for the
-    previous read-back (the outputs are reused)."""
-    ins, outs = device_tensors(cfg, data)
+    uploads its inputs and reads its result back.  The GEMM configurations
+    alternate two sets of device buffers, as a serving loop would: step i+1's
+    upload (its own stream) and step i-1's read-back (another stream; PCIe is
+    full duplex) overlap step i's compute, and a step waits only for its own
+    inputs and for the read-back that last used its buffers.  The quantiser and
+    MoE configurations keep one set (step i+1's upload waits for step i)."""
+    sets = [data, _clone_data(data)] if cfg in (0, 1, 2, 3, 4) else [data]
+    bufs = [device_tensors(cfg, d) for d in sets]
+    ins, outs = bufs[0]
     h_ins = [t.detach().cpu().pin_memory() for t in ins]
     h_outs = [torch.empty(t.shape, dtype=t.dtype).pin_memory() for t in outs]
     h2d, d2h = nbytes_of(ins), nbytes_of(outs)
-    call(cfg, data)
+    for d in sets:
+        call(cfg, d)
     torch.cuda.synchronize()
     s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
     es, ee = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     if pg:
         pg.barrier()
     torch.cuda.synchronize()
+    nb = len(sets)
     with gc_paused():
         es.record(stream)
         s_in.wait_event(es)
         s_out.wait_event(es)
-        done_out = None
-        for _ in range(args.e2e_steps):
-            with torch.cuda.stream(s_in):              # inputs are free once the last compute ended
-                s_in.wait_stream(stream)
-                for d, h in zip(ins, h_ins):
+        done_c = [None] * nb     # compute that last read buffer set b
+        done_out = [None] * nb   # read-back that last read buffer set b
+        last_out = None
+        for i in range(args.e2e_steps):
+            b = i % nb
+            d_ins, d_outs = bufs[b]
+            with torch.cuda.stream(s_in):              # the set's inputs are free once its last compute ended
+                if done_c[b] is not None:
+                    s_in.wait_event(done_c[b])
+                for d, h in zip(d_ins, h_ins):
                     d.copy_(h, non_blocking=True)
                 ev_in = torch.cuda.Event()
                 ev_in.record(s_in)
             stream.wait_event(ev_in)
-            if done_out is not None:
-                stream.wait_event(done_out)
-            call(cfg, data)
+            if done_out[b] is not None:
+                stream.wait_event(done_out[b])
+            call(cfg, sets[b])
             ev_c = torch.cuda.Event()
             ev_c.record(stream)
+            done_c[b] = ev_c
             with torch.cuda.stream(s_out):
                 s_out.wait_event(ev_c)
-                for h, d in zip(h_outs, outs):
+                for h, d in zip(h_outs, d_outs):
                     h.copy_(d, non_blocking=True)
-                done_out = torch.cuda.Event()
-                done_out.record(s_out)
-        stream.wait_event(done_out)
+                last_out = torch.cuda.Event()
+                last_out.record(s_out)
+                done_out[b] = last_out
+        stream.wait_event(last_out)
         ee.record(stream)
         torch.cuda.synchronize()
     t = all_max(pg, device, es.elapsed_time(ee) / 1e3)
@@ -895,7 +922,8 @@ def e2e_leg(cfg, data, args, device, stream, pg, flop_all, bytes_all):
     return {"value": round(v, 3), "unit": "GB/s" if quant else "TFLOP/s", "h2d_bytes_per_step": h2d,
             "d2h_bytes_per_step": d2h, "steps": args.e2e_steps,
             "api": "nvfp4_b200 public API (ctypes -> libnvfp4_b200.so)",
-            "copies": "pinned host; step i+1's upload overlaps step i's read-back"}
+            "copies": "pinned host; two device buffer sets (GEMM configurations): step i+1's upload and "
+                      "step i-1's read-back overlap step i's compute"}
 
 
 def shape_run(args, device):
