@@ -858,7 +858,9 @@ extern "C" int nvfp4_grouped_gemm(const nvfp4_group* groups, int num_groups, voi
   if (forced == 128 || forced == 256) bn = forced;
   // The CTA-pair kernel (256x256 tiles) when every group has at least 24 K
   // blocks and 256 columns, and covering the groups in 256-row pair blocks
-  // costs at most 1.5x the 128-row blocks' rows; it keeps one accumulator,
+  // costs at most 1.5x the 128-row blocks' rows (a last block of <= 128 rows
+  // runs as a half tile at ~0.95 of a full tile's time, so it counts as a
+  // full block); it keeps one accumulator,
   // so with few K blocks per tile its exposed epilogue loses.  Measured on
   // one B200 (us per call, pair / single-CTA): configuration 3 88.9 / 95.4,
   // configuration 4 241.8 / 255.0, 8 groups of 64-248 rows x 4096 x 7168
