@@ -29,7 +29,12 @@
 //   block: 8 + 16 KB of operands for 128 x 128 outputs).  Half tiles keep
 //   their place in the list, next to the group's other blocks of the same
 //   columns, which read the same B rows from L2; rows past M_g in a full
-//   tile's second CTA load as TMA zero fill and are not stored;
+//   tile's second CTA load as TMA zero fill and are not stored.  A loads as
+//   64-row boxes (two per full tile), so both tile kinds share one map.  A
+//   half tile does half a full tile's MMA work in ~0.95 of its time: with
+//   28 KB per stage in flight, the stage round trip paces its K blocks;
+// * a call of more than 48 groups is several launches; each later one is
+//   "chained" (it waits for the previous launch at its end, not its start);
 // * issue threads chosen with elect.sync, descriptors advanced from the
 //   stage-0 ones, one accumulator that the eight epilogue warps of each CTA
 //   pull into registers and release before the stores, all waits bounded.
