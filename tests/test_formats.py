@@ -93,6 +93,38 @@ def test_generate_group_input_layout():
     assert np.array_equal(logical, sfab[0][0].view(torch.uint8).numpy())
 
 
+def test_group_from_fp32_batched_layout():
+    """Batched (L = 2) grouped inputs from fp32: every tensor in the
+    reference's layout ([rows, K/2, L], K-major, L outermost in memory), each
+    batch slice bit-exact against the oracle quantiser, the permuted scales
+    the swizzle of the logical ones per batch, and a zero-row group kept."""
+    gen = torch.Generator().manual_seed(5)
+    shapes = [(130, 264, 512, 2), (0, 256, 256, 2), (64, 128, 256, 1)]
+    pairs = [(torch.randn(l, m, k, generator=gen), torch.randn(l, n, k, generator=gen))
+             for m, n, k, l in shapes]
+    abc, sfab, perm, sizes = I.group_from_fp32(pairs, device="cpu")
+    assert sizes == [(m, n, k, l) for m, n, k, l in shapes]
+    for (m, n, k, l), (a, b, c), (sa, sb), (pa, pb), (xa, xb) in zip(shapes, abc, sfab, perm, pairs):
+        assert a.shape == (m, k // 2, l) and b.shape == (n, k // 2, l) and c.shape == (m, n, l)
+        assert b.stride() == (k // 2, 1, n * k // 2)
+        if m:   # an empty tensor's strides are never read
+            assert a.stride() == (k // 2, 1, m * k // 2) and c.stride() == (n, 1, m * n)
+        assert sa.shape == (m, k // 16, l) and sb.shape == (n, k // 16, l)
+        for i in range(l):
+            want_b, want_sb = O.quantize_nvfp4(xb[i].numpy())
+            assert np.array_equal(b[:, :, i].view(torch.uint8).numpy(), want_b)
+            assert np.array_equal(sb[:, :, i].view(torch.uint8).numpy(), want_sb)
+            if m:
+                want_a, want_sa = O.quantize_nvfp4(xa[i].numpy())
+                assert np.array_equal(a[:, :, i].view(torch.uint8).numpy(), want_a)
+                assert np.array_equal(sa[:, :, i].view(torch.uint8).numpy(), want_sa)
+        for p_, s_, rows in ((pb, sb, n), (pa, sa, m)):
+            if rows == 0:
+                continue
+            mem = p_.view(torch.uint8).permute(5, 2, 4, 0, 1, 3).contiguous().numpy()
+            assert np.array_equal(O.unpermute_sf(mem, rows, k // 16), s_.view(torch.uint8).numpy())
+
+
 def test_config_samplers_are_fixed():
     m3 = I.config3_m_sizes()
     assert len(m3) == 8 and all(v % 64 == 0 and 64 <= v <= 2048 for v in m3)
