@@ -80,7 +80,7 @@ struct DeviceState {
   bool ready = false;
   int num_sms = 0;
   unsigned* status = nullptr;
-  bool smem_set[32] = {};  // one slot per kernel instantiation
+  std::atomic<bool> smem_set[32] = {};  // one slot per kernel instantiation (any thread may set it)
   int max_clusters[5] = {};  // co-resident clusters of the cluster split-K kernel, by size
   std::unordered_map<cudaStream_t, Workspace> ws;
   unsigned char* noalloc_scratch = nullptr;   // device address of g_noalloc_scratch
@@ -146,6 +146,15 @@ int get_device(DeviceState** out) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
   if (dev < 0 || dev >= kMaxDevices) return fail(NVFP4_ERR_DEVICE, "device index %d", dev);
+  // A thread that has made no runtime call yet has no current context, and
+  // the tensor-map encoder (a driver call) then fails: make the device's
+  // primary context current for this thread once.
+  thread_local int t_bound_dev = -1;
+  if (t_bound_dev != dev) {
+    e = cudaSetDevice(dev);
+    if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "cudaSetDevice(%d): %s", dev, cudaGetErrorString(e));
+    t_bound_dev = dev;
+  }
   std::lock_guard<std::mutex> lk(g_mu);
   DeviceState& d = g_dev[dev];
   if (!d.ready) {
@@ -278,11 +287,12 @@ int check_launch(const char* what) {
 
 template <typename Kern>
 int set_smem_once(DeviceState* d, int slot, Kern kern, int bytes) {
-  if (d->smem_set[slot]) return NVFP4_OK;
+  // two threads may both set the attribute the first time: it is idempotent
+  if (d->smem_set[slot].load(std::memory_order_acquire)) return NVFP4_OK;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess)
     return fail(NVFP4_ERR_CUDA, "cudaFuncSetAttribute(smem=%d): %s", bytes, cudaGetErrorString(e));
-  d->smem_set[slot] = true;
+  d->smem_set[slot].store(true, std::memory_order_release);
   return NVFP4_OK;
 }
 

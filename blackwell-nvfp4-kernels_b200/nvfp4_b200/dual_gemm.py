@@ -8,6 +8,7 @@ and c; the un-permuted scales are not needed.
 """
 from __future__ import annotations
 
+import threading
 import weakref
 
 import torch
@@ -109,10 +110,12 @@ class _Plan:
 
 _PLAN_SLOTS = 64        # >= the 15 rotating inputs of the reference's timing loop
 _plans: dict = {}
+_plans_lock = threading.Lock()   # host threads may insert concurrently; lookups need no lock
 
 
 def clear_plan_cache() -> None:
-    _plans.clear()
+    with _plans_lock:
+        _plans.clear()
 
 
 def dual_gemm(a, b1, b2, sfa_perm, sfb1_perm, sfb2_perm, c) -> torch.Tensor:
@@ -123,9 +126,10 @@ def dual_gemm(a, b1, b2, sfa_perm, sfb1_perm, sfb2_perm, c) -> torch.Tensor:
     if plan is None or not plan.matches(ts):
         m, n, k, l, dev = _validate(*ts)
         plan = _Plan(ts, (m, n, k, l), dev)
-        if len(_plans) >= _PLAN_SLOTS:
-            _plans.pop(next(iter(_plans)))
-        _plans[key] = plan
+        with _plans_lock:
+            if len(_plans) >= _PLAN_SLOTS:
+                _plans.pop(next(iter(_plans)))
+            _plans[key] = plan
     m, n, k, l = plan.sizes
     lib = _lib.load()
     _lib.check(on_device(plan.device,

@@ -14,6 +14,7 @@ C group table without re-validating; anything else is validated afresh.
 """
 from __future__ import annotations
 
+import threading
 import weakref
 
 import torch
@@ -76,6 +77,7 @@ class _Plan:
 
 
 _plans: dict = {}
+_plans_lock = threading.Lock()   # host threads may insert concurrently; lookups need no lock
 
 
 def _plan_for(abc, sf_perm, sizes):
@@ -85,14 +87,16 @@ def _plan_for(abc, sf_perm, sizes):
         return plan
     table, device = build_group_table(abc, sf_perm, sizes)
     plan = _Plan(abc, sf_perm, sizes, table, device)
-    if len(_plans) >= _PLAN_SLOTS:
-        _plans.pop(next(iter(_plans)))
-    _plans[key] = plan
+    with _plans_lock:
+        if len(_plans) >= _PLAN_SLOTS:
+            _plans.pop(next(iter(_plans)))
+        _plans[key] = plan
     return plan
 
 
 def clear_plan_cache() -> None:
-    _plans.clear()
+    with _plans_lock:
+        _plans.clear()
 
 
 def grouped_gemm(abc, sf_perm, sizes):

@@ -457,3 +457,54 @@ def test_device_quantisation_bit_exact():
     p, s = quantize_nvfp4(x.cuda())
     po, so = O.quantize_nvfp4(x.numpy())
     assert np.array_equal(s.cpu().numpy(), so) and np.array_equal(p.cpu().numpy(), po)
+
+
+def _clone(x):
+    if isinstance(x, torch.Tensor):
+        if x.element_size() == 1 and x.dtype != torch.uint8:
+            return x.view(torch.uint8).clone().view(x.dtype)
+        return x.clone()
+    if isinstance(x, (tuple, list)):
+        return type(x)(_clone(v) for v in x)
+    return x
+
+
+def test_two_host_threads_on_their_own_streams(monkeypatch):
+    """Two host threads, each on its own stream with its own buffers, run the
+    dual GEMM (workspace split-K forced: each stream has its own workspace)
+    and the grouped GEMM (CTA-pair kernel) interleaved; every output is
+    bit-identical to a single-threaded run."""
+    import threading
+    monkeypatch.setenv("NVFP4_DUAL_SPLITS", "3")
+    dual = I.generate_dual_input(256, 1024, 3072, 1, seed=21, device="cuda")
+    gen = torch.Generator().manual_seed(22)
+    group = I.group_from_fp32([(torch.randn(m, 6144, generator=gen), torch.randn(n, 6144, generator=gen))
+                               for m, n in ((300, 256), (128, 384), (512, 264))], device="cuda")
+    want_dual = D.custom_kernel(dual).clone()
+    want_group = [c.clone() for c in G.custom_kernel(group)]
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    sets = [(_clone(dual), _clone(group)) for _ in range(2)]
+    errors = []
+
+    def work(d, g):
+        try:
+            s = torch.cuda.Stream()
+            with torch.cuda.stream(s):
+                for _ in range(10):
+                    D.custom_kernel(d)
+                    G.custom_kernel(g)
+            s.synchronize()
+        except Exception as e:   # surfaced below
+            errors.append(e)
+
+    threads = [threading.Thread(target=work, args=st) for st in sets]
+    for t in threads:
+        t.start()
+    for t in threads:
+        t.join()
+    assert not errors, errors
+    assert _lib.device_status() == 0
+    for d, g in sets:
+        assert torch.equal(d[9], want_dual)
+        assert all(torch.equal(c, w) for (_, _, c), w in zip(g[0], want_group))
