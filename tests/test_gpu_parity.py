@@ -508,3 +508,47 @@ def test_two_host_threads_on_their_own_streams(monkeypatch):
     for d, g in sets:
         assert torch.equal(d[9], want_dual)
         assert all(torch.equal(c, w) for (_, _, c), w in zip(g[0], want_group))
+
+
+def _capture_and_replay(fn, outs):
+    """Eager result, then the same call captured in a CUDA graph (warmed up on
+    a side stream first, as torch documents) and replayed into zeroed outputs."""
+    fn()
+    torch.cuda.synchronize()
+    want = [o.clone() for o in outs]
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn()
+    torch.cuda.current_stream().wait_stream(s)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        fn()
+    for o in outs:
+        o.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    for o, w in zip(outs, want):
+        assert torch.equal(o, w)
+    del graph
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 4096, 7168), (512, 3072, 7168), (128, 7168, 16384), (1536, 512, 7168)])
+def test_dual_captured_in_a_cuda_graph(m, n, k):
+    """The dual GEMM under its automatic choice (CTA pair 64/128-wide, cluster
+    split-K) captured in a CUDA graph and replayed: bit-identical to eager."""
+    data = I.generate_dual_input(m, n, k, 1, seed=m + n, device="cuda")
+    _capture_and_replay(lambda: D.custom_kernel(data), [data[9]])
+
+
+@pytest.mark.parametrize("k,groups", [(6144, 60), (1024, 5)])
+def test_grouped_captured_in_a_cuda_graph(k, groups):
+    """The grouped GEMM captured in a CUDA graph: long K with more groups than
+    one launch holds (CTA-pair kernel, chained launches, half tiles) and short
+    K (single-CTA kernel); bit-identical to eager."""
+    gen = torch.Generator().manual_seed(k + groups)
+    shapes = [(64 * (i % 5 + 1), 256 + 8 * (i % 3)) for i in range(groups)]
+    data = I.group_from_fp32([(torch.randn(m, k, generator=gen), torch.randn(n, k, generator=gen))
+                              for m, n in shapes], device="cuda")
+    _capture_and_replay(lambda: G.custom_kernel(data), [c for _, _, c in data[0]])
