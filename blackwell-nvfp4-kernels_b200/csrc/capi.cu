@@ -74,6 +74,16 @@ struct Workspace {
   size_t partial_bytes = 0;
   int* counters = nullptr;
   size_t counter_count = 0;
+  bool zero_pending = false;   // new counters not yet zeroed by an uncaptured call
+};
+
+// One-time setup (context and symbol lookups, kernel attributes, workspace
+// allocation) may run while this thread captures a stream into a CUDA graph:
+// relaxed capture mode permits those calls for the scope of this guard.
+struct RelaxedCapture {
+  cudaStreamCaptureMode mode = cudaStreamCaptureModeRelaxed;
+  RelaxedCapture() { cudaThreadExchangeStreamCaptureMode(&mode); }
+  ~RelaxedCapture() { cudaThreadExchangeStreamCaptureMode(&mode); }
 };
 
 struct DeviceState {
@@ -151,6 +161,7 @@ int get_device(DeviceState** out) {
   // primary context current for this thread once.
   thread_local int t_bound_dev = -1;
   if (t_bound_dev != dev) {
+    RelaxedCapture relaxed;
     e = cudaSetDevice(dev);
     if (e != cudaSuccess) return fail(NVFP4_ERR_CUDA, "cudaSetDevice(%d): %s", dev, cudaGetErrorString(e));
     t_bound_dev = dev;
@@ -158,6 +169,7 @@ int get_device(DeviceState** out) {
   std::lock_guard<std::mutex> lk(g_mu);
   DeviceState& d = g_dev[dev];
   if (!d.ready) {
+    RelaxedCapture relaxed;
     int major = 0, minor = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
     cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
@@ -289,6 +301,7 @@ template <typename Kern>
 int set_smem_once(DeviceState* d, int slot, Kern kern, int bytes) {
   // two threads may both set the attribute the first time: it is idempotent
   if (d->smem_set[slot].load(std::memory_order_acquire)) return NVFP4_OK;
+  RelaxedCapture relaxed;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
   if (e != cudaSuccess)
     return fail(NVFP4_ERR_CUDA, "cudaFuncSetAttribute(smem=%d): %s", bytes, cudaGetErrorString(e));
@@ -297,30 +310,44 @@ int set_smem_once(DeviceState* d, int slot, Kern kern, int bytes) {
 }
 
 // Grow (never shrink) the stream's split-K scratch; counters start at zero
-// and every kernel leaves them at zero.
+// and every kernel leaves them at zero.  Growth may happen while the stream is
+// being captured into a CUDA graph: the allocation then runs in relaxed
+// capture mode, a buffer that is outgrown is kept (a graph captured earlier
+// may still use it), and new counters are zeroed by a stream-ordered memset —
+// a node of the graph when captured — on every call until an uncaptured call
+// has zeroed them.
 int get_workspace(DeviceState* d, cudaStream_t stream, size_t partial_bytes, size_t counters,
                   Workspace** out) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess) cs = cudaStreamCaptureStatusNone;
+  const bool capturing = cs != cudaStreamCaptureStatusNone;
   std::lock_guard<std::mutex> lk(g_mu);
   Workspace& w = d->ws[stream];
   if (w.partial_bytes < partial_bytes) {
-    if (w.partials) cudaFree(w.partials);
-    w.partials = nullptr;
-    w.partial_bytes = 0;
-    cudaError_t e = cudaMalloc(&w.partials, partial_bytes);
+    RelaxedCapture relaxed;
+    float* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, partial_bytes);
     if (e != cudaSuccess)
       return fail(NVFP4_ERR_CUDA, "split-K workspace (%zu bytes): %s", partial_bytes,
                   cudaGetErrorString(e));
+    w.partials = p;
     w.partial_bytes = partial_bytes;
   }
   if (w.counter_count < counters) {
-    if (w.counters) cudaFree(w.counters);
-    w.counters = nullptr;
-    w.counter_count = 0;
-    cudaError_t e = cudaMalloc(&w.counters, counters * sizeof(int));
-    if (e == cudaSuccess) e = cudaMemset(w.counters, 0, counters * sizeof(int));
+    RelaxedCapture relaxed;
+    int* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, counters * sizeof(int));
     if (e != cudaSuccess)
       return fail(NVFP4_ERR_CUDA, "split-K counters: %s", cudaGetErrorString(e));
+    w.counters = p;
     w.counter_count = counters;
+    w.zero_pending = true;
+  }
+  if (w.zero_pending) {
+    cudaError_t e = cudaMemsetAsync(w.counters, 0, w.counter_count * sizeof(int), stream);
+    if (e != cudaSuccess)
+      return fail(NVFP4_ERR_CUDA, "split-K counters: %s", cudaGetErrorString(e));
+    if (!capturing) w.zero_pending = false;
   }
   *out = &w;
   return NVFP4_OK;
@@ -338,6 +365,7 @@ void reset_workspaces(DeviceState* d) {
 int noalloc_scratch(DeviceState* d, unsigned char** out) {
   std::lock_guard<std::mutex> lk(g_mu);
   if (!d->noalloc_scratch) {
+    RelaxedCapture relaxed;
     void* ptr = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&ptr, g_noalloc_scratch);
     if (e != cudaSuccess || !ptr)

@@ -552,3 +552,11 @@ def test_grouped_captured_in_a_cuda_graph(k, groups):
     data = I.group_from_fp32([(torch.randn(m, k, generator=gen), torch.randn(n, k, generator=gen))
                               for m, n in shapes], device="cuda")
     _capture_and_replay(lambda: G.custom_kernel(data), [c for _, _, c in data[0]])
+
+
+def test_dual_workspace_split_captured_on_a_fresh_stream(monkeypatch):
+    """Workspace split-K (forced) captured in a CUDA graph: the capture stream
+    is new, so its workspace is created during the capture."""
+    monkeypatch.setenv("NVFP4_DUAL_SPLITS", "3")
+    data = I.generate_dual_input(256, 1024, 3072, 1, seed=77, device="cuda")
+    _capture_and_replay(lambda: D.custom_kernel(data), [data[9]])
