@@ -560,3 +560,31 @@ def test_dual_workspace_split_captured_on_a_fresh_stream(monkeypatch):
     monkeypatch.setenv("NVFP4_DUAL_SPLITS", "3")
     data = I.generate_dual_input(256, 1024, 3072, 1, seed=77, device="cuda")
     _capture_and_replay(lambda: D.custom_kernel(data), [data[9]])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_calls_on_a_device_other_than_the_current_one():
+    """Tensors on cuda:1 while cuda:0 is current (and the reverse): the
+    drop-ins run on the tensors' device, per-device state (status word,
+    kernel attributes, descriptors by address) stays apart, and the results
+    match the same call made on cuda:0."""
+    want = {}
+    for dev in (0, 1):
+        torch.cuda.set_device(0)
+        dual = I.generate_dual_input(256, 1024, 7168, 1, seed=31, device=f"cuda:{dev}")
+        gen = torch.Generator().manual_seed(32)
+        group = I.group_from_fp32([(torch.randn(m, 6144, generator=gen), torch.randn(256, 6144, generator=gen))
+                                   for m in (300, 100, 512)], device=f"cuda:{dev}")
+        if dev == 1:
+            torch.cuda.set_device(0)       # the current device is not the tensors'
+        out_d = D.custom_kernel(dual)
+        out_g = G.custom_kernel(group)
+        assert out_d.device.index == dev and all(c.device.index == dev for c in out_g)
+        torch.cuda.synchronize(dev)
+        want[dev] = (out_d.cpu(), [c.cpu() for c in out_g])
+    assert torch.equal(want[0][0], want[1][0])
+    assert all(torch.equal(a, b) for a, b in zip(want[0][1], want[1][1]))
+    assert torch.cuda.current_device() == 0
+    for dev in (0, 1):
+        with torch.cuda.device(dev):
+            assert _lib.device_status() == 0
