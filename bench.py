@@ -1009,11 +1009,26 @@ def main():
                             cpu_baseline=full))
             ok = True
             return
-        # the default suite: supporting lines first, the headline last
+        # the default suite: supporting lines first, the headline last.  On one
+        # GPU a supporting line that fails prints its error and the suite goes
+        # on to the headline (with several ranks every rank must take the same
+        # collective steps, so a failure there ends the run)
+        def extra(fn, what):
+            if world > 1:
+                return fn()
+            try:
+                return fn()
+            except Exception as e:   # reported on the line, not swallowed
+                emit({"metric": what, "error": f"{type(e).__name__}: {e}"[:400]})
+                torch.cuda.synchronize()
         for c in ((2, 3, 4) if world == 1 else (2, 4)):
-            emit(run_config(c, args, rank, world, device, pg, flush, e2e=full))
+            line = extra(lambda: run_config(c, args, rank, world, device, pg, flush, e2e=full),
+                         f"configuration {c}")
+            if line is not None:
+                emit(line)
         if world == 1:
-            for line in task_suite_lines(args, device):
+            lines = extra(lambda: list(task_suite_lines(args, device)), "task-suite geomeans")
+            for line in lines or []:
                 emit(line)
         else:
             line = run_config(1, args, rank, world, device, pg, flush, dual_scaling="weak", e2e=False)
