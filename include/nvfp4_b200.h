@@ -6,7 +6,10 @@
  * cudaStream_t passed as void* (NULL = legacy default stream).  Every entry
  * point returns NVFP4_OK (0) or a negative status; no exception crosses the
  * ABI.  Launches are asynchronous on `stream`; device-side wait timeouts are
- * reported through nvfp4_device_status().
+ * reported through nvfp4_device_status().  The calls work on the calling
+ * thread's current device; several host threads may call at once, each on
+ * its own stream; every call can be captured into a CUDA graph (the first
+ * one on a stream included).
  *
  * Data layouts are those of the reference task (nvfp4_dual_gemm/reference.py,
  * nvfp4_group_gemm/reference.py):
