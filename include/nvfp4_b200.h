@@ -64,8 +64,8 @@ int nvfp4_dual_gemm(const void* a, const void* b1, const void* b2, const void* s
  * in a fixed array inside this library (20 MiB of partials + 16 KiB of
  * counters, held by every GPU that loads the library until exit), and shapes
  * whose split needs more are rejected with NVFP4_ERR_SHAPE.  The first call on
- * a device looks up that array's device address; make that first call before
- * any stream capture.  All calls share the one array: calls that overlap on
+ * a device looks up that array's device address (also inside a stream
+ * capture).  All calls share the one array: calls that overlap on
  * the GPU (e.g. on two streams at once) race.  No counterpart in the
  * reference. */
 int nvfp4_dual_gemm_noalloc(const void* a, const void* b1, const void* b2, const void* sfa_perm,

@@ -90,3 +90,44 @@ def test_noalloc_rejects_shapes_beyond_its_scratch(lib, monkeypatch):
     assert st == _lib.NVFP4_ERR_SHAPE
     assert b"no-alloc scratch" in lib.nvfp4_last_error()
     assert _lib.device_status() == 0
+
+
+_FIRST_CALL_CAPTURED = r"""
+import sys, torch
+sys.path[:0] = ["blackwell-nvfp4-kernels_b200", "."]
+import os
+os.environ["NVFP4_DUAL_KERNEL"] = "single"
+from nvfp4_b200 import _lib, inputs as I
+lib = _lib.load()
+m, n, k = 128, 2048, 4096                     # K split through the fixed array
+d = I.generate_dual_input(m, n, k, 1, seed=12, device="cuda")
+args = lambda c: (d[0].data_ptr(), d[1].data_ptr(), d[2].data_ptr(), d[6].data_ptr(),
+                  d[7].data_ptr(), d[8].data_ptr(), c.data_ptr(), m, n, k, 1,
+                  torch.cuda.current_stream().cuda_stream)
+graph = torch.cuda.CUDAGraph()
+with torch.cuda.graph(graph):                 # this process's first no-alloc call
+    _lib.check(lib.nvfp4_dual_gemm_noalloc(*args(d[9])))
+d[9].zero_()
+graph.replay()
+torch.cuda.synchronize()
+want = torch.zeros_like(d[9])
+_lib.check(lib.nvfp4_dual_gemm(*args(want)))
+torch.cuda.synchronize()
+assert _lib.device_status() == 0
+assert torch.equal(d[9], want), "captured no-alloc call differs"
+del graph
+print("ok")
+"""
+
+
+def test_first_noalloc_call_inside_a_graph_capture():
+    """A fresh process whose first no-alloc call is captured into a CUDA graph
+    (the library looks up its fixed array during the capture): the replay
+    matches the ordinary entry point bit for bit."""
+    import subprocess
+    import sys
+    from pathlib import Path
+    root = Path(__file__).resolve().parent.parent
+    r = subprocess.run([sys.executable, "-c", _FIRST_CALL_CAPTURED], cwd=root, capture_output=True,
+                       text=True, timeout=600)
+    assert r.returncode == 0 and r.stdout.strip().endswith("ok"), (r.stdout[-2000:], r.stderr[-2000:])
